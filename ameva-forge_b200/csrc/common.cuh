@@ -1,0 +1,142 @@
+// Shared definitions of the forge_b200 CUDA library (sm_100a only).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <stdexcept>
+#include <string>
+
+#include "../../include/forge_b200.h"
+
+namespace fg {
+
+// Internal failures travel as exceptions and become a status code plus a
+// thread-local message at the C-ABI boundary (capi.cu).
+struct Error : std::runtime_error {
+  int status;
+  Error(int s, const std::string &m) : std::runtime_error(m), status(s) {}
+};
+
+[[noreturn]] inline void raise(int status, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  throw Error(status, buf);
+}
+
+// Sticky CUDA errors poison the context: they map to DeviceLost, the rest to
+// InternalGPU (the reference maps WebGPU "internal" scopes the same way,
+// graphExecutor.ts:1877-1933).
+inline bool cuda_error_is_sticky(cudaError_t e) {
+  switch (e) {
+    case cudaErrorIllegalAddress:
+    case cudaErrorIllegalInstruction:
+    case cudaErrorMisalignedAddress:
+    case cudaErrorInvalidAddressSpace:
+    case cudaErrorInvalidPc:
+    case cudaErrorLaunchFailure:
+    case cudaErrorHardwareStackError:
+    case cudaErrorAssert:
+    case cudaErrorLaunchTimeout:
+    case cudaErrorECCUncorrectable:
+    case cudaErrorDevicesUnavailable:
+      return true;
+    default:
+      return false;
+  }
+}
+
+[[noreturn]] inline void raise_cuda(cudaError_t e, const char *what, const char *file, int line) {
+  int st = e == cudaErrorMemoryAllocation ? FG_ERR_OUT_OF_MEMORY
+           : cuda_error_is_sticky(e)      ? FG_ERR_DEVICE_LOST
+           : (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver) ? FG_ERR_UNAVAILABLE
+                                                                          : FG_ERR_INTERNAL_GPU;
+  raise(st, "%s failed: %s (%s:%d)", what, cudaGetErrorString(e), file, line);
+}
+
+#define FG_CUDA(call)                                                      \
+  do {                                                                     \
+    cudaError_t fg_e_ = (call);                                            \
+    if (fg_e_ != cudaSuccess) ::fg::raise_cuda(fg_e_, #call, __FILE__, __LINE__); \
+  } while (0)
+
+#define FG_LAUNCH_CHECK() FG_CUDA(cudaGetLastError())
+
+#define FG_REQUIRE(cond, status, ...)          \
+  do {                                         \
+    if (!(cond)) ::fg::raise(status, __VA_ARGS__); \
+  } while (0)
+
+inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+inline uint64_t align_up(uint64_t a, uint64_t b) { return (a + b - 1) / b * b; }
+
+// ---------------------------------------------------------------- generator
+// splitmix64 counter generator + 4-term central-limit normal.  Every float
+// step is one explicitly rounded IEEE operation, so host and device agree bit
+// for bit with the CPU oracle's recipe.
+constexpr uint64_t kGolden = 0x9E3779B97F4A7C15ull;
+constexpr float kClt4Scale = 0x1.bb67aep-16f;  // 1/sqrt(4 (2^32 - 1) / 12)
+
+__host__ __device__ inline uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+__host__ __device__ inline uint64_t splitmix64(uint64_t seed, uint64_t i) { return mix64(seed + (i + 1) * kGolden); }
+
+__device__ inline float normal01(uint64_t seed, uint64_t i) {
+  uint64_t u = splitmix64(seed, i);
+  uint32_t s = (uint32_t)(u & 0xFFFF) + (uint32_t)((u >> 16) & 0xFFFF) + (uint32_t)((u >> 32) & 0xFFFF) +
+               (uint32_t)(u >> 48);
+  return __fmul_rn(__fsub_rn((float)s, 131070.0f), kClt4Scale);
+}
+
+// ---------------------------------------------------------------- quant layout
+// A quantized [N, K] matrix lives in one allocation:
+//   qs : the reference unpack packing (unpack_quant.wgsl.ts:38-51) --
+//        Q4_0: code of element i of a row in nibble i%8 of u32 word i/8
+//        (code = q + 8), Q8_0: byte i%4 of word i/4 (byte = q + 128);
+//   d  : fp16 scale per 32-element block, [N][K/32], 256-byte aligned.
+struct QMat {
+  const uint32_t *qs;
+  const __half *d;
+  int32_t qtype;  // FG_Q4_0 / FG_Q8_0
+  int64_t N, K;
+};
+inline uint64_t qmat_qs_bytes(int qtype, int64_t N, int64_t K) {
+  return (uint64_t)N * (uint64_t)K / (qtype == FG_Q4_0 ? 2 : 1);
+}
+inline uint64_t qmat_d_offset(int qtype, int64_t N, int64_t K) { return align_up(qmat_qs_bytes(qtype, N, K), 256); }
+inline uint64_t qmat_bytes(int qtype, int64_t N, int64_t K) {
+  return qmat_d_offset(qtype, N, K) + (uint64_t)N * (uint64_t)(K / 32) * 2;
+}
+inline int gguf_block_bytes(int qtype) { return qtype == FG_Q4_0 ? 18 : 34; }
+
+// ---------------------------------------------------------------- device helpers
+__device__ inline float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ inline float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Streaming 128-bit load that bypasses L1 allocation (weights are read once).
+__device__ inline uint4 ld_stream_u4(const void *p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+}  // namespace fg

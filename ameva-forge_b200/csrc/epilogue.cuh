@@ -1,0 +1,69 @@
+// Fused epilogues of the quantized GEMV / GEMM kernels.  Row n of W gives
+// output column n for token m; rows come in adjacent pairs (2i, 2i+1) so a
+// RoPE pair or a (gate, up) pair is finished by the thread holding both.
+#pragma once
+#include "runtime.cuh"
+
+namespace fg {
+
+// Interleaved-pair RoPE of one (v0, v1) pair: rope.wgsl.ts:45-59 (theta in fp32).
+__device__ inline void rope_pair(float v0, float v1, float inv_freq, int pos, float &o0, float &o1) {
+  float theta = __fmul_rn(inv_freq, (float)pos);
+  float s, c;
+  sincosf(theta, &s, &c);
+  o0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
+  o1 = __fadd_rn(__fmul_rn(v1, c), __fmul_rn(v0, s));
+}
+
+// SwiGLU: swiglu.wgsl.ts:38-40, gate / (1 + exp(-gate)) * up.
+__device__ inline float swiglu1(float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u); }
+
+// Store a finished pair of columns (n even, n+1) for token m.
+__device__ inline void epi_store_pair(const Epilogue &ep, int64_t n, int m, float v0, float v1) {
+  if (ep.mode == EPI_PLAIN) {
+    float *y = ep.y + (int64_t)m * ep.ldy + n;
+    if (ep.resid) {
+      const float *r = ep.resid + (int64_t)m * ep.ldy + n;
+      v0 = __fadd_rn(r[0], v0);
+      v1 = __fadd_rn(r[1], v1);
+    }
+    y[0] = v0;
+    y[1] = v1;
+  } else if (ep.mode == EPI_SWIGLU) {
+    ep.y[(int64_t)m * ep.ldy + (n >> 1)] = swiglu1(v0, v1);
+  } else {  // EPI_QKV
+    const int d = ep.head_dim;
+    const int b = m / ep.tokens_per_seq;
+    const int pos = ep.pos[b] + (m - b * ep.tokens_per_seq);
+    if (n < ep.n_q) {
+      float o0, o1;
+      rope_pair(v0, v1, ep.inv_freq[(n % d) >> 1], pos, o0, o1);
+      float *q = ep.q_out + (int64_t)m * ep.n_q + n;
+      q[0] = o0;
+      q[1] = o1;
+    } else {
+      const int64_t nk = n - ep.n_q;
+      const bool is_v = nk >= ep.n_kv;
+      const int64_t nn = is_v ? nk - ep.n_kv : nk;
+      const int hkv = ep.n_kv / d;
+      const int64_t hk = nn / d, c = nn % d;
+      const int64_t idx = (((int64_t)b * hkv + hk) * ep.cap + pos) * d + c;
+      if (is_v) {
+        *reinterpret_cast<__half2 *>(ep.v_cache + idx) = __halves2half2(__float2half_rn(v0), __float2half_rn(v1));
+      } else {
+        float o0, o1;
+        rope_pair(v0, v1, ep.inv_freq[c >> 1], pos, o0, o1);
+        *reinterpret_cast<__half2 *>(ep.k_cache + idx) = __halves2half2(__float2half_rn(o0), __float2half_rn(o1));
+      }
+    }
+  }
+}
+
+// Single column (PLAIN only; used when a kernel's row group is odd-sized).
+__device__ inline void epi_store_one(const Epilogue &ep, int64_t n, int m, float v) {
+  float *y = ep.y + (int64_t)m * ep.ldy + n;
+  if (ep.resid) v = __fadd_rn(ep.resid[(int64_t)m * ep.ldy + n], v);
+  *y = v;
+}
+
+}  // namespace fg

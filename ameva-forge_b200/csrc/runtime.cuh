@@ -1,0 +1,166 @@
+// Context, tensor registry, allocator and kernel launcher declarations.
+#pragma once
+
+#include <mutex>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+
+struct ncclComm;
+
+namespace fg {
+
+struct Tensor {
+  void *ptr = nullptr;
+  uint64_t bytes = 0;
+  int32_t dtype = FG_F32;
+  int32_t ndim = 0;
+  int64_t shape[FG_MAX_DIMS] = {0};
+  int64_t numel() const {
+    int64_t n = 1;
+    for (int i = 0; i < ndim; ++i) n *= shape[i];
+    return n;
+  }
+  QMat qmat() const {  // valid for FG_Q4_0 / FG_Q8_0 tensors of shape [N, K]
+    QMat q;
+    q.qtype = dtype;
+    q.N = shape[0];
+    q.K = shape[1];
+    q.qs = (const uint32_t *)ptr;
+    q.d = (const __half *)((const char *)ptr + qmat_d_offset(dtype, q.N, q.K));
+    return q;
+  }
+};
+
+// One context = one device, one stream, one handle namespace (the reference's
+// _globalRegistry + QuotaManager + device singleton, per GPU).
+struct Ctx {
+  int device = 0;
+  int tp_rank = 0, tp_size = 1;
+  cudaStream_t stream = nullptr;
+  cudaMemPool_t pool = nullptr;
+  ncclComm *nccl = nullptr;
+  std::recursive_mutex mu;
+  std::unordered_map<uint64_t, Tensor> tensors;
+  uint64_t next_id = 1;
+  uint64_t epoch = 1;  // bumped on context loss; handles of an old epoch are stale
+  uint64_t limit = 0, active = 0, pending = 0, peak = 0;
+  bool allow_non_finite = false;
+  bool lost = false;
+  // Pinned staging ring for host <-> device copies (buffers.ts:70-140 keeps a
+  // pow-2 staging pool; here two pinned halves alternate so the host copy of
+  // one chunk overlaps the DMA of the other).
+  void *staging[2] = {nullptr, nullptr};
+  cudaEvent_t staging_ev[2] = {nullptr, nullptr};
+  uint64_t staging_bytes = 0;
+  int num_sms = 148;
+
+  // allocation with quota accounting (quota.ts:65-313)
+  void *alloc(uint64_t bytes);
+  void free_async(void *p, uint64_t bytes);
+  fg_handle add(const Tensor &t);
+  Tensor &get(fg_handle h);
+  fg_handle make(const int64_t *shape, int ndim, int dtype, Tensor **out = nullptr);
+  void dispose(fg_handle h);
+  void h2d(void *dst, const void *src, uint64_t bytes);
+  void d2h(void *dst, const void *src, uint64_t bytes);
+  void sync();
+};
+
+uint64_t dtype_bytes(int dtype, int64_t numel, const int64_t *shape, int ndim);
+
+// ------------------------------------------------------------------ launchers
+// quant.cu
+void launch_unpack_quant(const uint32_t *packed, const float *scales, const float *zeros, int bits, int64_t gs,
+                         int64_t n, float *out, cudaStream_t s);
+// GGUF blocks of an [N, K] matrix into rows r * dst_rs + dst_ro of dst.
+void launch_gguf_to_device(const uint8_t *blocks, int qtype, int64_t N, int64_t K, const QMat &dst, int64_t dst_rs,
+                           int64_t dst_ro, cudaStream_t s);
+void launch_device_to_gguf(const QMat &w, uint8_t *blocks, cudaStream_t s);
+void launch_dequant(const QMat &w, float *out, cudaStream_t s);
+void launch_synth_normal(uint64_t seed, uint64_t offset, int64_t n, float mean, float stdv, int dtype, void *out,
+                         cudaStream_t s);
+// Synthetic [N, K] block of a [*, k_full] matrix starting at (row0, col0),
+// written into rows r * dst_rs + dst_ro of dst.
+void launch_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, int64_t row0, int64_t col0, int64_t k_full,
+                        float stdv, const QMat &dst, int64_t dst_rs, int64_t dst_ro, cudaStream_t s);
+
+// Fused epilogues shared by the GEMV and GEMM kernels.  Row n of the weight
+// produces column n of y for token m.
+enum EpiMode { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_QKV = 2 };
+struct Epilogue {
+  int mode = EPI_PLAIN;
+  float *y = nullptr;            // PLAIN: [M][ldy]; SWIGLU: [M][ldy] (N/2 columns used)
+  const float *resid = nullptr;  // PLAIN only: y = resid + acc (may alias y)
+  int64_t ldy = 0;
+  // QKV: rows [0,n_q) -> q_out (rope), [n_q, n_q+n_kv) -> k cache (rope, fp16),
+  // [n_q+n_kv, n_q+2 n_kv) -> v cache (fp16).
+  float *q_out = nullptr;  // [M][n_q]
+  __half *k_cache = nullptr, *v_cache = nullptr;  // [B][Hkv][cap][d]
+  int n_q = 0, n_kv = 0, head_dim = 0, cap = 0;
+  int tokens_per_seq = 1;        // token m belongs to sequence m / tokens_per_seq
+  const int *pos = nullptr;      // [B] cache length before this forward
+  const float *inv_freq = nullptr;  // [head_dim/2]
+};
+
+// gemv.cu: y = x W^T for up to 4 rows of x (the batch-1 decode path).
+// x [M][K] fp32; optional fused RMSNorm of x (gamma may be null).
+bool gemv_supported(const QMat &w, int M);
+void launch_qgemv(const QMat &w, const float *x, int M, const float *norm_gamma, float norm_eps, bool do_norm,
+                  const Epilogue &ep, int num_sms, cudaStream_t s);
+// gemm.cu: the same contract for any M (prefill / batched decode).
+void launch_qgemv_ld(const QMat &w, const float *x, int M, int64_t ldx, const float *norm_gamma, float norm_eps,
+                     bool do_norm, const Epilogue &ep, int num_sms, cudaStream_t s);
+// gemm.cu: the same contract without the fused norm, any M (prefill / batched decode).
+void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, int num_sms, cudaStream_t s);
+void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s);
+
+// attention.cu
+struct AttnArgs {
+  const void *q;  // fp32 or fp16
+  const void *k, *v;
+  float *o;
+  int q_f16 = 0, kv_f16 = 0;
+  int B = 1, H = 1, Hkv = 1, Nq = 1, d = 64;
+  int64_t q_sb = 0, q_sh = 0, q_si = 0;  // element strides of Q (batch, head, token)
+  int64_t o_sb = 0, o_sh = 0, o_si = 0;
+  int64_t kv_sb = 0, kv_sh = 0;          // element strides of K/V (batch, head); token stride = d
+  const int *n_kv_dev = nullptr;         // per-sequence live KV length on the device (or null)
+  int n_kv = 0;                          // used when n_kv_dev is null
+  int n_kv_add = 0;                      // n_kv = n_kv_dev[b] + n_kv_add
+  float scale = 1.0f;
+  int causal = 0;
+  int scratch_batch = 0;                 // decode scratch was sized for this batch (0 = B)
+};
+void launch_attention(const AttnArgs &a, int num_sms, cudaStream_t s);
+bool attn_decode_supported(const AttnArgs &a);
+// Split-KV decode attention (Nq == 1, fp16 cache, fp32 q).  Needs a scratch
+// area of attn_decode_scratch_bytes() bytes: per-head arrival counters first
+// (sized for scratch_batch, zero on entry and left zero on exit), then the
+// per-split partial results.
+int attn_decode_splits(const AttnArgs &a, int max_kv, int num_sms);
+uint64_t attn_decode_scratch_bytes(const AttnArgs &a, int splits);
+void launch_attention_decode(const AttnArgs &a, int splits, void *scratch, cudaStream_t s);
+
+// misc.cu
+void launch_rmsnorm(const float *x, int64_t ldx, const float *gamma, float eps, int64_t tokens, int64_t dim,
+                    float *out, cudaStream_t s);
+void launch_rope(const float *x, int64_t rows, int64_t N, int64_t d, const float *inv_freq, int64_t offset,
+                 float *out, cudaStream_t s);
+void launch_swiglu(const float *g, const float *u, int64_t n, float *out, cudaStream_t s);
+void launch_embedding(const void *table, int table_f16, int64_t vocab, int64_t dim, const void *ids, int ids_f32,
+                      int64_t n, float *out, cudaStream_t s);
+void launch_add(const float *a, const float *b, int64_t n, float *out, cudaStream_t s);
+void launch_argmax(const float *logits, int64_t rows, int64_t n, int64_t ld, int32_t *out, cudaStream_t s);
+// per-row (value, index) keys for a cross-rank greedy pick: key orders by value
+// then by lower global index; index_base = first global column of this shard.
+void launch_argmax_keys(const float *logits, int64_t rows, int64_t n, int64_t ld, int64_t index_base,
+                        unsigned long long *keys, cudaStream_t s);
+void launch_keys_to_ids(const unsigned long long *keys, int64_t rows, int32_t *ids, cudaStream_t s);
+void launch_cast(const void *in, int in_dtype, void *out, int out_dtype, int64_t n, cudaStream_t s);
+void launch_check_finite(const float *x, int64_t n, int *flag, cudaStream_t s);
+void launch_advance_pos(int *pos, int batch, int by, int32_t *log, const int32_t *ids, int *step, int log_steps,
+                        cudaStream_t s);
+
+}  // namespace fg

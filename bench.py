@@ -1,0 +1,362 @@
+"""Benchmark: Q4_0 Llama-2-7B-shaped greedy decode, batch 1, KV context 4096.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+One process per GPU (torchrun for N > 1); the model is tensor-parallel over
+the N GPUs (NCCL all-reduce after o_proj and down_proj), so the total work per
+step is fixed (strong scaling).  A step = one decode token of every sequence.
+
+  value  : tokens/s with the step loop resident on the device (token ids stay
+           in HBM, K CUDA-graph launches back to back), timed with CUDA events
+           on the library's stream, max over ranks;
+  e2e    : the same metric through the public C ABI call (fg_llama_decode) with
+           host buffers: each step copies the input id in and the next id out;
+  roofline: the fused dequant-GEMV (the dominant kernel) re-timed live on the
+           7B layer shapes with cold L2, algorithmic bytes / launch time vs the
+           measured HBM copy bandwidth;
+  cpu_baseline: the CPU oracle (a port of the reference arithmetic) decoding
+           a bounded sample of the same workload on the host cores.
+
+Weights are seeded synthetic N(0, 0.02) quantized to GGUF Q4_0; the prompt is
+4096 seeded random ids (no checkpoint or dataset is used).
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "ameva-forge_b200"))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402  (plumbing: rendezvous, barriers, events on the library stream)
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "Q4_0 decode tokens/s"
+UNIT = "tokens/s"
+CONTEXT = 4096
+BATCH = 1
+SEED = 20240601
+SHAPE = dict(vocab_size=32000, hidden_size=4096, intermediate_size=11008, num_hidden_layers=32,
+             num_attention_heads=32, num_key_value_heads=32, rms_norm_eps=1e-5, rope_theta=10000.0)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="forge_b200", choices=["forge_b200", "reference"])
+    ap.add_argument("--cpu-baseline", type=int, default=1, help="time the CPU oracle sample (rank 0, N=1)")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def config_block(n):
+    return {"workload": "llama2-7b-shape q4_0 greedy decode", "model": "Llama-2-7B-shaped (random init)",
+            "global_batch": BATCH, "context": CONTEXT, "seq_len": CONTEXT, "layers": 32, "hidden": 4096,
+            "heads": 32, "head_dim": 128, "ffn": 11008, "vocab": 32000, "weights": "GGUF Q4_0",
+            "kv_cache": "fp16", "parallelism": f"tp{n}",
+            "l2": "inputs larger than L2: every step streams 3.7 GB of weights + 2.1 GB of KV"}
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.rows = []
+        if self.p is None:
+            return
+        self.p.terminate()
+        try:
+            out, _ = self.p.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.p.kill()
+            out, _ = self.p.communicate()
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9:
+                self.rows.append(f)
+
+    def summary(self):
+        if not getattr(self, "rows", None):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------ CPU oracle
+def cpu_sample(steps=2, layers=2):
+    """Decode `steps` tokens at context 4096 through `layers` of the 32 layers
+    (+ embedding and lm_head) with the CPU oracle; KV filled with seeded
+    fp16-rounded N(0,1) values.  Returns tokens/s scaled to the full model."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+    shp = O.LlamaShape(**{**SHAPE, "num_hidden_layers": layers})
+    w = O.synth_llama(shp, SEED)
+    ref = O.LlamaRef(w, max_seq=CONTEXT + steps + 1, kv_f16=True)
+    for li in range(layers):
+        n = CONTEXT * shp.num_key_value_heads * shp.head_dim
+        kv = O.round_f16(O.normal(SEED + li, 0, n, 0.0, 1.0)).reshape(shp.num_key_value_heads, CONTEXT, shp.head_dim)
+        ref.k[li][0, :, :CONTEXT] = kv
+        ref.v[li][0, :, :CONTEXT] = kv[:, ::-1]
+    ref.pos = CONTEXT
+    tok = np.array([[1]], np.int32)
+    t_layers, t_head = 0.0, 0.0
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        lg = ref.forward(tok)
+        t_all = time.perf_counter() - t0
+        # split: lm_head + embedding cost measured separately once
+        t_layers += t_all
+        tok = np.array([[O.argmax(lg[0, -1])]], np.int32)
+    # lm_head + final norm cost, to scale only the layer part
+    x = O.normal(1, 0, shp.hidden_size, 0.0, 1.0).reshape(1, shp.hidden_size)
+    t0 = time.perf_counter()
+    O.qmatmul(w.qtype, w.lm_head, shp.vocab_size, shp.hidden_size, O.rmsnorm(x, w.norm))
+    t_head = time.perf_counter() - t0
+    per_tok = (t_layers / steps - t_head) * (32 / layers) + t_head
+    return {"value": 1.0 / per_tok, "unit": UNIT, "cores": O.num_threads(), "kind": "port",
+            "sample": f"{steps} decode steps at context {CONTEXT} through {layers} of 32 layers + lm_head, "
+                      f"layer time scaled x{32 // layers}; KV filled with seeded fp16 N(0,1)"}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's arithmetic on the host cores (the
+    oracle port; the reference itself runs only through WebGPU in a browser)."""
+    if rank != 0:
+        return
+    res = None
+    for _ in range(args.warmup and 1):
+        pass
+    t0 = time.perf_counter()
+    samples = [cpu_sample(steps=max(1, min(args.steps, 3)))]
+    wall = time.perf_counter() - t0
+    res = samples[0]
+    line = {"impl": "reference", "metric": METRIC, "value": res["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / res["value"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic", "config": config_block(world),
+            "cpu_baseline": {"value": res["value"], "unit": UNIT, "cores": res["cores"], "kind": res["kind"],
+                             "sample": res["sample"]},
+            "e2e": {"value": res["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "wall_s": wall}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ roofline
+def gemv_roofline(ctx, world, reps=8):
+    """Time the fused dequant-GEMV alone on this rank's 7B shard shapes with
+    cold L2 (rotating over `reps` weight copies of each shape, > 2x L2)."""
+    import forge_b200  # noqa: F401
+    H, I, V, d = 4096, 11008, 32000, 128
+    shapes = [((3 * 32 // world) * d, H), (H, 32 // world * d), (2 * I // world, H), (H, I // world)]
+    ws, xs = [], {}
+    for si, (N, K) in enumerate(shapes):
+        for r in range(reps):
+            ws.append((ctx.synth_quant("Q4_0", N, K, seed=1000 * si + r, std=0.02), N, K))
+        xs[K] = ctx.synth_normal((1, K), np.float32, seed=K)
+    stream = torch.cuda.ExternalStream(ctx_stream(ctx))
+    outs = []
+    for h, N, K in ws[:4]:  # warm up every instantiation
+        outs.append(ctx.qmatmul(xs[K], h))
+    ctx.synchronize()
+    for o in outs:
+        ctx.dispose(o)
+    total_bytes, total_ms, launches = 0, 0.0, 0
+    per_shape = []
+    for si in range(len(shapes)):
+        group = [w for w in ws if (w[1], w[2]) == shapes[si]]
+        N, K = shapes[si]
+        with torch.cuda.stream(stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            outs = [ctx.qmatmul(xs[K], h) for h, _, _ in group]
+            e1.record()
+        e1.synchronize()
+        ms = e0.elapsed_time(e1)
+        b = len(group) * (N * K // 32 * 18 + 4 * (K + N))
+        per_shape.append({"N": N, "K": K, "us_per_launch": 1000 * ms / len(group),
+                          "GBps": b / (ms / 1e3) / 1e9})
+        total_bytes += b
+        total_ms += ms
+        launches += len(group)
+        for o in outs:
+            ctx.dispose(o)
+    for h, _, _ in ws:
+        ctx.dispose(h)
+    for x in xs.values():
+        ctx.dispose(x)
+    ctx.synchronize()
+    return total_bytes / launches, total_ms / launches, per_shape
+
+
+def ctx_stream(ctx):
+    import ctypes
+    from forge_b200 import _capi as C
+    s = ctypes.c_void_p()
+    C.call("fg_get_stream", ctx.ptr, ctypes.byref(s))
+    return s.value
+
+
+def measured_peak():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def ncu_traffic():
+    """dram bytes per GEMV launch from the committed ncu summary, if any."""
+    p = os.path.join(REPO, "profiles", "qgemv_q4_0_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return None
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if world > 1 and not dist.is_initialized():
+        torch.cuda.set_device(local)
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    import forge_b200
+    nid = None
+    if world > 1:
+        obj = [forge_b200.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        nid = obj[0]
+    ctx = forge_b200.Context(device=local, tp_rank=rank, tp_size=world, nccl_id=nid)
+    cap = CONTEXT + args.warmup + 2 * args.steps + 8
+    cfg = forge_b200.LlamaConfig(max_position_embeddings=cap, max_batch=BATCH, qtype="Q4_0", **SHAPE)
+    model = forge_b200.LlamaForCausalLM(cfg, ctx)
+    t0 = time.perf_counter()
+    model.synthesize(SEED)
+    t_synth = time.perf_counter() - t0
+    rng = np.random.default_rng(SEED)
+    prompt = rng.integers(0, SHAPE["vocab_size"], (BATCH, CONTEXT), dtype=np.int32)
+    t0 = time.perf_counter()
+    _, nxt = model.forward(prompt, return_logits=False)
+    t_prefill = time.perf_counter() - t0
+
+    stream = torch.cuda.ExternalStream(ctx_stream(ctx))
+    model.generate_device(BATCH, args.warmup)  # warm-up steps (graph capture + W launches)
+    ctx.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # ---- value: device-resident decode loop ----
+    barrier()
+    ctx.synchronize()
+    with Clocks(local) as clk:
+        with torch.cuda.stream(stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        model.generate_device(BATCH, args.steps, read=False)  # enqueues K graph launches
+        with torch.cuda.stream(stream):
+            e1.record()
+        ctx.synchronize()
+        ms = e0.elapsed_time(e1)
+    toks = model.read_tokens(BATCH, args.steps)
+    barrier()
+    t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = args.steps * BATCH / (ms / 1e3)
+
+    # ---- e2e: public API with host buffers, one call per step ----
+    ids = np.asarray(toks[-1], np.int32).copy()
+    barrier()
+    ctx.synchronize()
+    with torch.cuda.stream(stream):
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record()
+    for _ in range(args.steps):
+        ids = model.decode(ids)  # H2D of the ids, graph launch, D2H of the next ids
+    with torch.cuda.stream(stream):
+        f1.record()
+    ctx.synchronize()
+    ms_e2e = f0.elapsed_time(f1)
+    t = torch.tensor([ms_e2e], dtype=torch.float64, device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_value = args.steps * BATCH / (float(t.item()) / 1e3)
+
+    # ---- roofline of the dominant kernel ----
+    b_launch, ms_launch, per_shape = gemv_roofline(ctx, world)
+    peak, peak_kind = measured_peak()
+    achieved = b_launch / (ms_launch / 1e3) / 1e9
+    traffic = ncu_traffic()
+
+    model.close()
+    ctx.shutdown()
+    cpu = None
+    if rank == 0 and world == 1 and args.cpu_baseline:
+        cpu = cpu_sample()
+    if rank == 0:
+        L = SHAPE["num_hidden_layers"]
+        launches = (5 * L + 4 + (1 if world > 1 else 0)) * args.steps
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "config": config_block(world),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * BATCH,
+                    "d2h_bytes_per_step": 4 * BATCH},
+            "roofline": {"bound": "hbm", "kernel": "k_qgemv (fused Q4_0 dequant-GEMV)", "achieved": achieved,
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
+                         "algorithmic_bytes_per_launch": b_launch, "us_per_launch": ms_launch * 1e3,
+                         "per_shape": per_shape},
+            "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
+            "setup": {"synthesize_s": t_synth, "prefill_s": t_prefill, "prefill_tokens": CONTEXT * BATCH},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

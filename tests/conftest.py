@@ -18,3 +18,19 @@ def pytest_configure(config):
 def golden():
     import numpy as np
     return np.load(os.path.join(REPO, "tests", "golden", "reference_golden.npz"))
+
+
+@pytest.fixture(scope="session")
+def ctx():
+    """One device context for the GPU tests (the library's default)."""
+    import forge_b200
+    c = forge_b200.Context(device=0)
+    yield c
+    c.shutdown()
+
+
+def max_rel_err(out, ref):
+    """max |out - ref| / max |ref| -- the tolerance measure of the parity bar."""
+    import numpy as np
+    ref = np.asarray(ref, np.float64)
+    return float(np.abs(np.asarray(out, np.float64) - ref).max() / max(np.abs(ref).max(), 1e-30))

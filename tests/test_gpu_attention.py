@@ -1,0 +1,59 @@
+"""Flash attention vs the reference fixtures (fp32, atol 1e-4 as the
+reference's own suite) and the oracle (fp16 inputs, 2e-3 * ||ref||_inf)."""
+import numpy as np
+import pytest
+
+import inputs as I
+import oracle as O
+from conftest import max_rel_err
+from forge_b200.errors import AMEVAForgeShapeError
+
+pytestmark = pytest.mark.gpu
+
+
+def test_mha_golden(ctx, golden):
+    q, k, v = I.mha()
+    out = ctx.read(ctx.flashAttention(ctx.upload(q), ctx.upload(k), ctx.upload(v), isCausal=False))
+    np.testing.assert_allclose(out, golden["mha_out"], atol=1e-4)
+
+
+def test_gqa_causal_golden(ctx, golden):
+    q, k, v = I.gqa()
+    out = ctx.read(ctx.flashAttention(ctx.upload(q), ctx.upload(k), ctx.upload(v), isCausal=True))
+    np.testing.assert_allclose(out, golden["gqa_out"], atol=1e-4)
+
+
+@pytest.mark.parametrize("B,H,Hkv,Nq,Nkv,d,causal", [
+    (1, 4, 4, 1, 37, 64, True),      # decode row against a KV offset
+    (2, 8, 2, 5, 70, 128, True),     # chunked prefill with KV offset
+    (1, 2, 1, 33, 33, 256, False),   # max head dim
+    (1, 2, 2, 3, 2, 8, True),        # fewer keys than queries: early rows see none
+    (3, 2, 2, 17, 17, 32, True),
+])
+def test_fp32_ragged_vs_oracle(ctx, B, H, Hkv, Nq, Nkv, d, causal):
+    q = O.normal(1, 0, B * H * Nq * d).reshape(B, H, Nq, d)
+    k = O.normal(2, 0, B * Hkv * Nkv * d).reshape(B, Hkv, Nkv, d)
+    v = O.normal(3, 0, B * Hkv * Nkv * d).reshape(B, Hkv, Nkv, d)
+    out = ctx.read(ctx.flashAttention(ctx.upload(q), ctx.upload(k), ctx.upload(v), isCausal=causal))
+    np.testing.assert_allclose(out, O.attention(q, k, v, causal=causal), atol=2e-5)
+
+
+def test_fp16_prefill_vs_oracle(ctx):
+    B, H, S, d = 1, 4, 512, 128
+    q16 = O.f32_to_f16(O.normal(11, 0, B * H * S * d)).reshape(B, H, S, d)
+    k16 = O.f32_to_f16(O.normal(12, 0, B * H * S * d)).reshape(B, H, S, d)
+    v16 = O.f32_to_f16(O.normal(13, 0, B * H * S * d)).reshape(B, H, S, d)
+    out = ctx.read(ctx.flashAttention(ctx.upload(q16.view(np.float16)), ctx.upload(k16.view(np.float16)),
+                                      ctx.upload(v16.view(np.float16)), scale=1 / np.sqrt(d), isCausal=True))
+    ref = O.attention(O.f16_to_f32(q16), O.f16_to_f32(k16), O.f16_to_f32(v16), 1 / np.sqrt(d), True)
+    assert max_rel_err(out, ref) <= 2e-3
+
+
+def test_validation_messages(ctx):
+    q = ctx.upload(np.zeros((1, 3, 4, 8), np.float32))
+    k = ctx.upload(np.zeros((1, 2, 4, 8), np.float32))
+    with pytest.raises(AMEVAForgeShapeError, match="divisible"):
+        ctx.flashAttention(q, k, k)
+    big = ctx.upload(np.zeros((1, 1, 1, 264), np.float32))
+    with pytest.raises(AMEVAForgeShapeError, match="256"):
+        ctx.flashAttention(big, big, big)

@@ -1,0 +1,114 @@
+"""Elementwise / row ops of the op API vs the reference fixtures and oracle."""
+import numpy as np
+import pytest
+
+import inputs as I
+import oracle as O
+from forge_b200.errors import AMEVAForgeShapeError, AMEVAForgeValidationError
+
+pytestmark = pytest.mark.gpu
+
+
+def test_rmsnorm_golden(ctx, golden):
+    x, g = I.rmsnorm()
+    out = ctx.read(ctx.rmsNorm(ctx.upload(x), ctx.upload(g), 1e-5))
+    np.testing.assert_allclose(out, golden["rmsnorm_out"], rtol=1e-5, atol=1e-6)
+    x, g = I.rmsnorm_small()
+    np.testing.assert_allclose(ctx.read(ctx.rmsNorm(ctx.upload(x), ctx.upload(g))), golden["rmsnorm2_out"],
+                               rtol=1e-5, atol=1e-6)
+    # no gamma
+    np.testing.assert_allclose(ctx.read(ctx.rmsNorm(ctx.upload(x))), O.rmsnorm(x, None), rtol=1e-5, atol=1e-6)
+
+
+def test_rope_golden(ctx, golden):
+    np.testing.assert_allclose(ctx.read(ctx.rope(ctx.upload(I.rope()), 10000.0, 0)), golden["rope_out"], atol=1e-5)
+    out = ctx.read(ctx.rope(ctx.upload(I.rope_offset()), 10000.0, 2047))
+    np.testing.assert_allclose(out, O.rope(I.rope_offset(), 10000.0, 2047), atol=2e-6)
+    np.testing.assert_allclose(out, golden["rope_off_out"], atol=5e-4)
+
+
+def test_swiglu_golden(ctx, golden):
+    gt, up = I.swiglu()
+    np.testing.assert_allclose(ctx.read(ctx.swiglu(ctx.upload(gt), ctx.upload(up))), golden["swiglu_out"],
+                               rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("shape", I.MATMUL_SHAPES)
+def test_matmul_golden(ctx, golden, shape):
+    M, K, N = shape
+    A, B = I.matmul(M, K, N)
+    out = ctx.read(ctx.matmul(ctx.upload(A), ctx.upload(B)))
+    np.testing.assert_allclose(out, golden[f"matmul_{M}x{K}x{N}"], atol=1e-4, rtol=1e-4)
+
+
+def test_embedding_zero_rows_for_bad_ids(ctx):
+    table = O.normal(1, 0, 50 * 64, 0.0, 1.0).reshape(50, 64)
+    ids = np.array([[0, 49, 50, -1], [7, 3, 1000, 2]], np.int32)
+    out = ctx.read(ctx.embedding(ctx.upload(table), ctx.upload(ids)))
+    assert out.shape == (2, 4, 64)
+    assert np.array_equal(out, O.embedding(table, ids))
+    fids = np.array([0.4, 1.5, 2.5, np.nan, 49.6, -0.4], np.float32)  # WGSL round(): half to even
+    ctx.configure_runtime(allow_non_finite=True)
+    try:
+        outf = ctx.read(ctx.embedding(ctx.upload(table), ctx.upload(fids)))
+    finally:
+        ctx.configure_runtime(allow_non_finite=False)
+    expect = O.embedding(table, np.array([0, 2, 2, -1, 50, 0], np.int32))
+    assert np.array_equal(outf, expect)
+    t16 = O.f32_to_f16(table)
+    out16 = ctx.read(ctx.embedding(ctx.upload(t16.view(np.float16)), ctx.upload(ids)))
+    assert np.array_equal(out16, O.embedding(O.f16_to_f32(t16), ids))
+
+
+def test_argmax_tie_and_nan_rules(ctx):
+    assert ctx.read(ctx.argmax(ctx.upload(I.GREEDY_LOGITS)))[0] == I.GREEDY_INDEX
+    ctx.configure_runtime(allow_non_finite=True)
+    try:
+        rows = np.array([[3.0, 7.0, 7.0, 1.0], [np.nan, 9.0, 2.0, 1.0], [1.0, np.nan, 5.0, 5.0],
+                         [-np.inf, -np.inf, -np.inf, -np.inf]], np.float32)
+        got = ctx.read(ctx.argmax(ctx.upload(rows)))
+    finally:
+        ctx.configure_runtime(allow_non_finite=False)
+    assert got.tolist() == [O.argmax(r) for r in rows] == [1, 0, 2, 0]
+    big = O.normal(5, 0, 3 * 32000, 0.0, 1.0).reshape(3, 32000)
+    big[1, 31999] = 100.0
+    big[2, 5] = big[2, 77] = 100.0
+    assert ctx.read(ctx.argmax(ctx.upload(big))).tolist() == [O.argmax(r) for r in big]
+
+
+def test_add_and_cast(ctx):
+    a, b = O.normal(1, 0, 1000, 0, 1), O.normal(2, 0, 1000, 0, 1)
+    assert np.array_equal(ctx.read(ctx.add(ctx.upload(a), ctx.upload(b))), a + b)
+    h = ctx.cast(ctx.upload(a), np.float16)
+    assert np.array_equal(ctx.read(h).view(np.uint16), O.f32_to_f16(a))
+
+
+def test_upload_rejects_non_finite(ctx):
+    with pytest.raises(AMEVAForgeValidationError):
+        ctx.upload(np.array([1.0, np.inf], np.float32))
+
+
+def test_dispose_and_quota(ctx):
+    from forge_b200.errors import AMEVAForgeDisposedError
+    q0 = ctx.quota()
+    h = ctx.upload(np.zeros(1 << 20, np.float32))
+    assert ctx.quota()["active"] >= q0["active"] + 4 * (1 << 20)
+    ctx.dispose(h)
+    ctx.dispose(h)  # double dispose is a no-op
+    with pytest.raises(AMEVAForgeDisposedError):
+        ctx.read(h)
+    assert ctx.quota()["active"] == q0["active"]
+
+
+def test_quota_exceeded():
+    import forge_b200
+    from forge_b200.errors import AMEVAForgeQuotaExceededError
+    with forge_b200.Context(device=0, vram_limit_bytes=64 << 20) as small:
+        with pytest.raises(AMEVAForgeQuotaExceededError):
+            small.empty((64 << 20,), np.float32)
+        small.empty((1 << 20,), np.float32)
+
+
+def test_shape_errors(ctx):
+    with pytest.raises(AMEVAForgeShapeError):
+        ctx.matmul(ctx.upload(np.zeros((2, 3), np.float32)), ctx.upload(np.zeros((4, 2), np.float32)))
