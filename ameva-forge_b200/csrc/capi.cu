@@ -128,6 +128,18 @@ void Ctx::d2h(void *dst, const void *src, uint64_t bytes) {
 void Ctx::sync() {
   FG_CUDA(cudaStreamSynchronize(stream));
   pending = 0;
+  check_device_error();
+}
+
+void Ctx::check_device_error() {
+  if (!gemv.err) return;
+  int e = 0;
+  FG_CUDA(cudaMemcpy(&e, gemv.err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e != 0) {
+    int zero = 0;
+    FG_CUDA(cudaMemcpy(gemv.err, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    raise(FG_ERR_INTERNAL_GPU, "a kernel wait timed out on the device (code %d); results of the step are invalid", e);
+  }
 }
 
 // inv_freq tables for standalone RoPE calls, cached per (base, d).
@@ -287,6 +299,17 @@ int fg_init(const fg_init_opts *opts, fg_ctx **out) {
     FG_CUDA(cudaEventCreateWithFlags(&c.staging_ev[i], cudaEventDisableTiming));
     FG_CUDA(cudaEventRecord(c.staging_ev[i], c.stream));
   }
+  {  // GEMV workspace: 4 Mi partial floats, 64 Ki tickets, the error word
+    c.gemv.part_floats = 4ull << 20;
+    c.gemv.n_tickets = 1 << 16;
+    const uint64_t bytes = c.gemv.part_floats * 4 + (uint64_t)c.gemv.n_tickets * 4 + 256;
+    char *p = (char *)c.alloc(bytes);
+    FG_CUDA(cudaMemsetAsync(p, 0, bytes, c.stream));
+    c.gemv.part = (float *)p;
+    c.gemv.tickets = (int *)(p + c.gemv.part_floats * 4);
+    c.gemv.err = (int *)(p + c.gemv.part_floats * 4 + (uint64_t)c.gemv.n_tickets * 4);
+    FG_CUDA(cudaStreamSynchronize(c.stream));
+  }
   if (c.tp_size > 1) {
     ncclUniqueId id;
     std::memcpy(&id, opts->nccl_id, 128);
@@ -309,6 +332,7 @@ int fg_shutdown(fg_ctx *ctx) {
     cudaSetDevice(c.device);
     cudaStreamSynchronize(c.stream);
     for (auto &kv : c.tensors) cudaFreeAsync(kv.second.ptr, c.stream);
+    if (c.gemv.part) cudaFreeAsync(c.gemv.part, c.stream);
     c.tensors.clear();
     auto it = g_rope.find(&c);
     if (it != g_rope.end()) {
@@ -399,6 +423,7 @@ int fg_upload_quant(fg_ctx *ctx, int32_t qtype, const void *gguf_blocks, uint64_
   const int64_t shape[2] = {rows, cols};
   Tensor *t = nullptr;
   const fg_handle h = c.make(shape, 2, qtype, &t);
+  FG_CUDA(cudaMemsetAsync(t->ptr, 0, t->bytes, c.stream));  // defined scale padding
   if (need) {
     void *tmp = c.alloc(need);
     c.h2d(tmp, gguf_blocks, need);
@@ -512,35 +537,62 @@ int fg_dequant(fg_ctx *ctx, fg_handle w, fg_handle *out) {
   FG_API_END
 }
 
+namespace {
+// Validates x [..., K] against W [N, K]; returns M (rows of x).
+int64_t qmatmul_rows(const Tensor &xt, const Tensor &wt) {
+  check_f32(xt, "qmatmul activations");
+  FG_REQUIRE(is_quant(wt.dtype), FG_ERR_DTYPE, "qmatmul: weight must be Q4_0/Q8_0");
+  const int64_t K = wt.shape[1];
+  FG_REQUIRE(xt.ndim >= 1 && xt.shape[xt.ndim - 1] == K, FG_ERR_SHAPE, "qmatmul: x[..., %lld] vs W[%lld, %lld]",
+             (long long)(xt.ndim ? xt.shape[xt.ndim - 1] : 0), (long long)wt.shape[0], (long long)K);
+  const int64_t M = K ? xt.numel() / K : 0;
+  FG_REQUIRE(M <= INT32_MAX, FG_ERR_SHAPE, "qmatmul: too many rows");
+  return M;
+}
+
+void qmatmul_launch(Ctx &c, const Tensor &xt, const QMat &q, int64_t M, float *y) {
+  Epilogue ep;
+  ep.mode = EPI_PLAIN;
+  ep.y = y;
+  ep.ldy = q.N;
+  if (M == 0 || q.N == 0) return;
+  if (gemv_supported(q, (int)M))
+    launch_qgemv_ld(q, (const float *)xt.ptr, (int)M, q.K, nullptr, 0.0f, false, ep, c.gemv, c.num_sms, c.stream);
+  else
+    launch_qgemm(q, (const float *)xt.ptr, (int)M, q.K, ep, c.num_sms, c.stream);
+}
+}  // namespace
+
 int fg_qmatmul(fg_ctx *ctx, fg_handle x, fg_handle w, fg_handle *out) {
   FG_API_BEGIN
   Guard g(ctx);
   Ctx &c = C(ctx);
   Tensor &xt = c.get(x);
   Tensor &wt = c.get(w);
-  check_f32(xt, "qmatmul activations");
-  FG_REQUIRE(is_quant(wt.dtype), FG_ERR_DTYPE, "qmatmul: weight must be Q4_0/Q8_0");
+  const int64_t M = qmatmul_rows(xt, wt);
   const QMat q = wt.qmat();
-  FG_REQUIRE(xt.ndim >= 1 && xt.shape[xt.ndim - 1] == q.K, FG_ERR_SHAPE, "qmatmul: x[..., %lld] vs W[%lld, %lld]",
-             (long long)(xt.ndim ? xt.shape[xt.ndim - 1] : 0), (long long)q.N, (long long)q.K);
-  const int64_t M = q.K ? xt.numel() / q.K : 0;
   int64_t shp[FG_MAX_DIMS];
   for (int i = 0; i < xt.ndim; ++i) shp[i] = xt.shape[i];
   shp[xt.ndim - 1] = q.N;
   Tensor *o = nullptr;
   const fg_handle h = c.make(shp, xt.ndim, FG_F32, &o);
-  Epilogue ep;
-  ep.mode = EPI_PLAIN;
-  ep.y = (float *)o->ptr;
-  ep.ldy = q.N;
-  if (M > 0 && q.N > 0) {
-    FG_REQUIRE(M <= INT32_MAX, FG_ERR_SHAPE, "qmatmul: too many rows");
-    if (gemv_supported(q, (int)M))
-      launch_qgemv(q, (const float *)xt.ptr, (int)M, nullptr, 0.0f, false, ep, c.num_sms, c.stream);
-    else
-      launch_qgemm(q, (const float *)xt.ptr, (int)M, q.K, ep, c.num_sms, c.stream);
-  }
+  qmatmul_launch(c, c.get(x), q, M, (float *)o->ptr);
   *out = h;
+  FG_API_END
+}
+
+int fg_qmatmul_into(fg_ctx *ctx, fg_handle x, fg_handle w, fg_handle out) {
+  FG_API_BEGIN
+  Guard g(ctx);
+  Ctx &c = C(ctx);
+  Tensor &xt = c.get(x);
+  Tensor &wt = c.get(w);
+  Tensor &ot = c.get(out);
+  const int64_t M = qmatmul_rows(xt, wt);
+  const QMat q = wt.qmat();
+  FG_REQUIRE(ot.dtype == FG_F32 && ot.numel() == M * q.N, FG_ERR_SHAPE, "qmatmul_into: output must be F32 [.., %lld]",
+             (long long)q.N);
+  qmatmul_launch(c, xt, q, M, (float *)ot.ptr);
   FG_API_END
 }
 
@@ -763,6 +815,7 @@ int fg_synth_quant(fg_ctx *ctx, int32_t qtype, int64_t rows, int64_t cols, uint6
   const int64_t shp[2] = {rows, cols};
   Tensor *o = nullptr;
   const fg_handle h = c.make(shp, 2, qtype, &o);
+  FG_CUDA(cudaMemsetAsync(o->ptr, 0, o->bytes, c.stream));
   launch_synth_quant(qtype, rows, cols, seed, row0, 0, cols, stdv, o->qmat(), 1, 0, c.stream);
   *out = h;
   FG_API_END

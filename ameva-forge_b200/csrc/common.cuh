@@ -99,22 +99,51 @@ __device__ inline float normal01(uint64_t seed, uint64_t i) {
 
 // ---------------------------------------------------------------- quant layout
 // A quantized [N, K] matrix lives in one allocation:
-//   qs : the reference unpack packing (unpack_quant.wgsl.ts:38-51) --
-//        Q4_0: code of element i of a row in nibble i%8 of u32 word i/8
-//        (code = q + 8), Q8_0: byte i%4 of word i/4 (byte = q + 128);
-//   d  : fp16 scale per 32-element block, [N][K/32], 256-byte aligned.
+//   qs : Q8_0 -- the reference unpack packing (unpack_quant.wgsl.ts:44-51):
+//        byte i%4 of u32 word i/4 holds q + 128 for element i of the row;
+//        Q4_0 -- codes (q + 8) regrouped for the tensor-core GEMV fragments:
+//        a row holds its blocks rounded up to a multiple of 4 (zero padded);
+//        the 4 words of block b sit at word (b/4)*16 + t*4 + b%4, and word t
+//        holds, in nibbles 0..7, the codes of block elements
+//        2t, 2t+8, 16+2t, 24+2t, 2t+1, 2t+9, 17+2t, 25+2t (q4_elem);
+//   d  : fp16 scale per 32-element block, [N][ldd], 256-byte aligned; rows
+//        padded to a multiple of 8 scales (16 bytes) for the TMA row pitch.
 struct QMat {
   const uint32_t *qs;
   const __half *d;
   int32_t qtype;  // FG_Q4_0 / FG_Q8_0
   int64_t N, K;
+  int64_t ldd;        // scales per d row (K/32 rounded up to 8)
+  int64_t row_words;  // u32 words per qs row
 };
+__host__ __device__ inline int64_t qmat_ldd(int64_t K) { return (K / 32 + 7) / 8 * 8; }
+__host__ __device__ inline int64_t qmat_row_words(int qtype, int64_t K) {
+  return qtype == FG_Q4_0 ? (K / 32 + 3) / 4 * 16 : K / 4;
+}
+// Block element held by nibble p of word t (Q4_0 device packing).
+__host__ __device__ inline int q4_elem(int t, int p) {
+  const int base = (p & 3) == 0 ? 0 : (p & 3) == 1 ? 8 : (p & 3) == 2 ? 16 : 24;
+  return base + 2 * t + (p >> 2);
+}
+// Word (within the row) holding lane-word t of block b (Q4_0 device packing).
+__host__ __device__ inline int64_t q4_word(int64_t b, int t) { return (b >> 2) * 16 + t * 4 + (b & 3); }
 inline uint64_t qmat_qs_bytes(int qtype, int64_t N, int64_t K) {
-  return (uint64_t)N * (uint64_t)K / (qtype == FG_Q4_0 ? 2 : 1);
+  return (uint64_t)N * (uint64_t)qmat_row_words(qtype, K) * 4;
 }
 inline uint64_t qmat_d_offset(int qtype, int64_t N, int64_t K) { return align_up(qmat_qs_bytes(qtype, N, K), 256); }
 inline uint64_t qmat_bytes(int qtype, int64_t N, int64_t K) {
-  return qmat_d_offset(qtype, N, K) + (uint64_t)N * (uint64_t)(K / 32) * 2;
+  return qmat_d_offset(qtype, N, K) + (uint64_t)N * (uint64_t)qmat_ldd(K) * 2;
+}
+inline QMat qmat_at(void *base, int qtype, int64_t N, int64_t K) {
+  QMat q;
+  q.qtype = qtype;
+  q.N = N;
+  q.K = K;
+  q.ldd = qmat_ldd(K);
+  q.row_words = qmat_row_words(qtype, K);
+  q.qs = (const uint32_t *)base;
+  q.d = (const __half *)((const char *)base + qmat_d_offset(qtype, N, K));
+  return q;
 }
 inline int gguf_block_bytes(int qtype) { return qtype == FG_Q4_0 ? 18 : 34; }
 

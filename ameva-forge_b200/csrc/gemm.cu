@@ -46,26 +46,22 @@ __global__ void __launch_bounds__(256) k_qgemm_simt(QMat w, const float *__restr
     {
       const int r = tid >> 2, t = tid & 3;
       const int64_t n = n0 + r;
-      float v[8];
-      if (n < w.N) {
-        const float sc = __half2float(w.d[n * nb + kb]);
-        if (w.qtype == FG_Q4_0) {
-          const uint32_t word = w.qs[(n * nb + kb) * 4 + t];
+      const float sc = n < w.N ? __half2float(w.d[n * w.ldd + kb]) : 0.0f;
+      if (w.qtype == FG_Q4_0) {
+        const uint32_t word = n < w.N ? w.qs[n * w.row_words + q4_word(kb, t)] : 0x88888888u;
 #pragma unroll
-          for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(__fsub_rn((float)((word >> (4 * k)) & 0xFu), 8.0f), sc);
-        } else {
-          const uint2 wd = reinterpret_cast<const uint2 *>(w.qs)[(n * nb + kb) * 4 + t];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) v[k] = __fmul_rn(__fsub_rn((float)((wd.x >> (8 * k)) & 0xFFu), 128.0f), sc);
-#pragma unroll
-          for (int k = 0; k < 4; ++k) v[4 + k] = __fmul_rn(__fsub_rn((float)((wd.y >> (8 * k)) & 0xFFu), 128.0f), sc);
-        }
+        for (int p = 0; p < 8; ++p)
+          ws[q4_elem(t, p)][r] = __fmul_rn(__fsub_rn((float)((word >> (4 * p)) & 0xFu), 8.0f), sc);
       } else {
+        const uint2 wd = n < w.N ? reinterpret_cast<const uint2 *>(w.qs + n * w.row_words)[kb * 4 + t]
+                                 : make_uint2(0x80808080u, 0x80808080u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = 0.0f;
+        for (int k = 0; k < 4; ++k)
+          ws[8 * t + k][r] = __fmul_rn(__fsub_rn((float)((wd.x >> (8 * k)) & 0xFFu), 128.0f), sc);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          ws[8 * t + 4 + k][r] = __fmul_rn(__fsub_rn((float)((wd.y >> (8 * k)) & 0xFFu), 128.0f), sc);
       }
-#pragma unroll
-      for (int k = 0; k < 8; ++k) ws[8 * t + k][r] = v[k];
     }
     __syncthreads();
 #pragma unroll 8

@@ -81,14 +81,10 @@ namespace {
 uint64_t tensor_seed(uint64_t model_seed, int layer, int tid) { return splitmix64(model_seed, (uint64_t)layer * 16 + tid); }
 
 QMat make_qmat(fg_llama *m, int qtype, int64_t N, int64_t K) {
-  void *p = m->dalloc(qmat_bytes(qtype, N, K));
-  QMat q;
-  q.qtype = qtype;
-  q.N = N;
-  q.K = K;
-  q.qs = (const uint32_t *)p;
-  q.d = (const __half *)((char *)p + qmat_d_offset(qtype, N, K));
-  return q;
+  const uint64_t bytes = qmat_bytes(qtype, N, K);
+  void *p = m->dalloc(bytes);
+  FG_CUDA(cudaMemsetAsync(p, 0, bytes, m->ctx->stream));  // defined scale padding
+  return qmat_at(p, qtype, N, K);
 }
 
 void allreduce(fg_llama *m, float *buf, int64_t n) {
@@ -103,7 +99,7 @@ void linear(fg_llama *m, const QMat &w, const float *x, int M, int64_t ldx, cons
             const Epilogue &ep) {
   Ctx &c = *m->ctx;
   if (gemv_supported(w, M)) {
-    launch_qgemv_ld(w, x, M, ldx, gamma, m->cfg.rms_norm_eps, do_norm, ep, c.num_sms, c.stream);
+    launch_qgemv_ld(w, x, M, ldx, gamma, m->cfg.rms_norm_eps, do_norm, ep, c.gemv, c.num_sms, c.stream);
   } else {
     const float *xx = x;
     int64_t ld = ldx;
@@ -553,6 +549,7 @@ int fg_llama_decode(fg_llama *m, const int32_t *ids, int32_t batch, int32_t *nex
   m->last_batch = batch;
   if (logits) read_logits(m, batch, logits);
   if (next_ids) c.d2h(next_ids, m->ids, (uint64_t)batch * 4);
+  if (logits || next_ids) c.check_device_error();
   FG_LAPI_END
 }
 
@@ -576,6 +573,7 @@ int fg_llama_tokens(fg_llama *m, int32_t *host, int64_t count) {
   LGuard g(m);
   FG_REQUIRE(count >= 0 && count <= (int64_t)m->log_steps * m->max_batch, FG_ERR_SHAPE, "token count out of range");
   m->ctx->d2h(host, m->token_log, (uint64_t)count * 4);
+  m->ctx->check_device_error();
   FG_LAPI_END
 }
 

@@ -5,6 +5,24 @@
 
 namespace fg {
 
+// Q4_0 device packing (common.cuh): codes of one 32-element block <-> its 4
+// lane words.
+__device__ __forceinline__ void q4_pack(const uint8_t code[32], uint32_t w[4]) {
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int p = 0; p < 8; ++p) v |= (uint32_t)(code[q4_elem(t, p)] & 0xF) << (4 * p);
+    w[t] = v;
+  }
+}
+__device__ __forceinline__ void q4_unpack(const uint32_t w[4], uint8_t code[32]) {
+#pragma unroll
+  for (int t = 0; t < 4; ++t)
+#pragma unroll
+    for (int p = 0; p < 8; ++p) code[q4_elem(t, p)] = (w[t] >> (4 * p)) & 0xF;
+}
+
 // ---------------------------------------------------------------------------
 // UNPACK_QUANT_WGSL main (packages/forge/src/tensor/kernels/unpack_quant.wgsl.ts:
 // 25-62) with the graph path's dispatch (graphExecutor.ts:1313-1323):
@@ -49,32 +67,28 @@ void launch_unpack_quant(const uint32_t *packed, const float *scales, const floa
 // One thread per block; the 18/34-byte source blocks are read bytewise.
 // ---------------------------------------------------------------------------
 __global__ void k_gguf_to_device(const uint8_t *__restrict__ src, int qtype, int64_t nblocks, int64_t nbr,
-                                 int64_t dst_rs, int64_t dst_ro, uint32_t *__restrict__ qs, __half *__restrict__ d) {
+                                 int64_t ldd, int64_t row_words, int64_t dst_rs, int64_t dst_ro,
+                                 uint32_t *__restrict__ qs, __half *__restrict__ d) {
   for (int64_t sb = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; sb < nblocks; sb += (int64_t)gridDim.x * blockDim.x) {
     // source block sb = (row r, column block cb); destination row r * dst_rs + dst_ro
-    const int64_t b = ((sb / nbr) * dst_rs + dst_ro) * nbr + sb % nbr;
+    const int64_t drow = (sb / nbr) * dst_rs + dst_ro, cb = sb % nbr;
+    const int64_t b = drow * nbr + cb;      // qs block index
+    const int64_t db = drow * ldd + cb;     // scale index (padded rows)
     const int64_t src_b = sb;
     if (qtype == FG_Q4_0) {
       const uint8_t *blk = src + 18 * src_b;
-      uint8_t q[16];
+      uint8_t code[32];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) q[j] = blk[2 + j];
-      uint4 w;
-      uint32_t ws[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        uint32_t word = 0;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          int e = 8 * t + k;
-          uint32_t code = e < 16 ? (q[e] & 0xFu) : (q[e - 16] >> 4);
-          word |= code << (4 * k);
-        }
-        ws[t] = word;
+      for (int j = 0; j < 16; ++j) {
+        code[j] = blk[2 + j] & 0xF;
+        code[j + 16] = blk[2 + j] >> 4;
       }
-      w.x = ws[0]; w.y = ws[1]; w.z = ws[2]; w.w = ws[3];
-      reinterpret_cast<uint4 *>(qs)[b] = w;
-      d[b] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
+      uint32_t ws[4];
+      q4_pack(code, ws);
+      uint32_t *row = qs + drow * row_words;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) row[q4_word(cb, t)] = ws[t];
+      d[db] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
     } else {
       const uint8_t *blk = src + 34 * src_b;
       uint32_t ws[8];
@@ -88,7 +102,7 @@ __global__ void k_gguf_to_device(const uint8_t *__restrict__ src, int qtype, int
       uint4 *o = reinterpret_cast<uint4 *>(qs) + 2 * b;
       o[0] = make_uint4(ws[0], ws[1], ws[2], ws[3]);
       o[1] = make_uint4(ws[4], ws[5], ws[6], ws[7]);
-      d[b] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
+      d[db] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
     }
   }
 }
@@ -100,28 +114,28 @@ void launch_gguf_to_device(const uint8_t *blocks, int qtype, int64_t N, int64_t 
   FG_REQUIRE(dst.K == K && dst.qtype == qtype && (N - 1) * dst_rs + dst_ro < dst.N, FG_ERR_SHAPE,
              "quant repack: destination does not fit");
   int grid = (int)std::min<int64_t>(ceil_div(nb, 256), 148 * 16);
-  k_gguf_to_device<<<grid, 256, 0, s>>>(blocks, qtype, nb, K / 32, dst_rs, dst_ro, const_cast<uint32_t *>(dst.qs),
-                                        const_cast<__half *>(dst.d));
+  k_gguf_to_device<<<grid, 256, 0, s>>>(blocks, qtype, nb, K / 32, dst.ldd, dst.row_words, dst_rs, dst_ro,
+                                        const_cast<uint32_t *>(dst.qs), const_cast<__half *>(dst.d));
   FG_LAUNCH_CHECK();
 }
 
 __global__ void k_device_to_gguf(const uint32_t *__restrict__ qs, const __half *__restrict__ d, int qtype,
-                                 int64_t nblocks, uint8_t *__restrict__ dst) {
+                                 int64_t nblocks, int64_t nbr, int64_t ldd, int64_t row_words,
+                                 uint8_t *__restrict__ dst) {
   for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks; b += (int64_t)gridDim.x * blockDim.x) {
-    unsigned short dh = __half_as_ushort(d[b]);
+    unsigned short dh = __half_as_ushort(d[(b / nbr) * ldd + b % nbr]);
     if (qtype == FG_Q4_0) {
       uint8_t *blk = dst + 18 * b;
       blk[0] = dh & 0xFF;
       blk[1] = dh >> 8;
       uint32_t ws[4];
-      uint4 w = reinterpret_cast<const uint4 *>(qs)[b];
-      ws[0] = w.x; ws[1] = w.y; ws[2] = w.z; ws[3] = w.w;
+      const uint32_t *row = qs + (b / nbr) * row_words;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        uint32_t lo = (ws[j / 8] >> (4 * (j % 8))) & 0xFu;
-        uint32_t hi = (ws[(j + 16) / 8] >> (4 * ((j + 16) % 8))) & 0xFu;
-        blk[2 + j] = (uint8_t)(lo | (hi << 4));
-      }
+      for (int t = 0; t < 4; ++t) ws[t] = row[q4_word(b % nbr, t)];
+      uint8_t code[32];
+      q4_unpack(ws, code);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) blk[2 + j] = (uint8_t)(code[j] | (code[j + 16] << 4));
     } else {
       uint8_t *blk = dst + 34 * b;
       blk[0] = dh & 0xFF;
@@ -137,42 +151,49 @@ void launch_device_to_gguf(const QMat &w, uint8_t *blocks, cudaStream_t s) {
   int64_t nb = w.N * (w.K / 32);
   if (nb == 0) return;
   int grid = (int)std::min<int64_t>(ceil_div(nb, 256), 148 * 16);
-  k_device_to_gguf<<<grid, 256, 0, s>>>(w.qs, w.d, w.qtype, nb, blocks);
+  k_device_to_gguf<<<grid, 256, 0, s>>>(w.qs, w.d, w.qtype, nb, w.K / 32, w.ldd, w.row_words, blocks);
   FG_LAUNCH_CHECK();
 }
 
 // ---------------------------------------------------------------------------
 // Exact dequantisation to fp32 [N, K]: (code - zero) * f32(d) with the same two
 // roundings as the reference unpack on the mapped operands (zero 8 / 128).
-// One thread per 8 output values; 2 x 16-byte stores.
+// One thread per 32-value block; 8 x 16-byte stores.
 // ---------------------------------------------------------------------------
-__global__ void k_dequant(const uint32_t *__restrict__ qs, const __half *__restrict__ d, int qtype, int64_t n8,
-                          float *__restrict__ out) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
-    float sc = __half2float(d[i / 4]);  // 4 groups of 8 per 32-element block
-    float v[8];
+__global__ void k_dequant(const uint32_t *__restrict__ qs, const __half *__restrict__ d, int qtype, int64_t nblocks,
+                          int64_t nbr, int64_t ldd, int64_t row_words, float *__restrict__ out) {
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks; b += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = b / nbr, cb = b % nbr;
+    const float sc = __half2float(d[r * ldd + cb]);
+    const uint32_t *row = qs + r * row_words;
+    float v[32];
     if (qtype == FG_Q4_0) {
-      uint32_t w = qs[i];
+      uint32_t ws[4];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = __fmul_rn(__fsub_rn((float)((w >> (4 * k)) & 0xFu), 8.0f), sc);
+      for (int t = 0; t < 4; ++t) ws[t] = row[q4_word(cb, t)];
+      uint8_t code[32];
+      q4_unpack(ws, code);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __fmul_rn(__fsub_rn((float)code[j], 8.0f), sc);
     } else {
-      uint2 w = reinterpret_cast<const uint2 *>(qs)[i];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) v[k] = __fmul_rn(__fsub_rn((float)((w.x >> (8 * k)) & 0xFFu), 128.0f), sc);
+      for (int t = 0; t < 8; ++t) {
+        const uint32_t w = row[cb * 8 + t];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) v[4 + k] = __fmul_rn(__fsub_rn((float)((w.y >> (8 * k)) & 0xFFu), 128.0f), sc);
+        for (int k = 0; k < 4; ++k) v[4 * t + k] = __fmul_rn(__fsub_rn((float)((w >> (8 * k)) & 0xFFu), 128.0f), sc);
+      }
     }
-    float4 *o = reinterpret_cast<float4 *>(out + 8 * i);
-    o[0] = make_float4(v[0], v[1], v[2], v[3]);
-    o[1] = make_float4(v[4], v[5], v[6], v[7]);
+    float4 *o = reinterpret_cast<float4 *>(out + 32 * b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
   }
 }
 
 void launch_dequant(const QMat &w, float *out, cudaStream_t s) {
-  int64_t n8 = w.N * w.K / 8;
-  if (n8 == 0) return;
-  int grid = (int)std::min<int64_t>(ceil_div(n8, 256), 148 * 16);
-  k_dequant<<<grid, 256, 0, s>>>(w.qs, w.d, w.qtype, n8, out);
+  const int64_t nb = w.N * (w.K / 32);
+  if (nb == 0) return;
+  int grid = (int)std::min<int64_t>(ceil_div(nb, 128), 148 * 16);
+  k_dequant<<<grid, 128, 0, s>>>(w.qs, w.d, w.qtype, nb, w.K / 32, w.ldd, w.row_words, out);
   FG_LAUNCH_CHECK();
 }
 
@@ -202,13 +223,14 @@ void launch_synth_normal(uint64_t seed, uint64_t offset, int64_t n, float mean, 
 // N01(seed, (row0 + r) * K + c)).  Q4_0: d = v_absmax / -8, code =
 // min(15, trunc(v / d + 8.5)); Q8_0: d = absmax / 127, q = round(v / d).
 __global__ void k_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, int64_t row0, int64_t col0,
-                              int64_t k_full, float stdv, int64_t dst_rs, int64_t dst_ro,
-                              uint32_t *__restrict__ qs, __half *__restrict__ dsc) {
+                              int64_t k_full, float stdv, int64_t dst_rs, int64_t dst_ro, int64_t ldd,
+                              int64_t row_words, uint32_t *__restrict__ qs, __half *__restrict__ dsc) {
   const int64_t nbr = K / 32;
   const int64_t nb = N * nbr;
   for (int64_t sb = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; sb < nb; sb += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = sb / nbr, cb = sb % nbr;
     const int64_t b = (r * dst_rs + dst_ro) * nbr + cb;
+    const int64_t db = (r * dst_rs + dst_ro) * ldd + cb;
     const uint64_t base = (uint64_t)(row0 + r) * (uint64_t)k_full + (uint64_t)col0 + (uint64_t)cb * 32;
     float v[32];
     float amax = 0.0f, vmax = 0.0f;
@@ -224,15 +246,18 @@ __global__ void k_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, in
     if (qtype == FG_Q4_0) {
       float dd = __fdiv_rn(vmax, -8.0f);
       float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
-      uint32_t w[4] = {0, 0, 0, 0};
+      uint8_t code[32];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
         int c = __float2int_rz(__fadd_rn(__fmul_rn(v[j], id), 8.5f));
-        c = c > 15 ? 15 : c;
-        w[j / 8] |= (uint32_t)c << (4 * (j % 8));
+        code[j] = (uint8_t)(c > 15 ? 15 : c);
       }
-      reinterpret_cast<uint4 *>(qs)[b] = make_uint4(w[0], w[1], w[2], w[3]);
-      dsc[b] = __float2half_rn(dd);
+      uint32_t w[4];
+      q4_pack(code, w);
+      uint32_t *row = qs + (r * dst_rs + dst_ro) * row_words;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) row[q4_word(cb, t)] = w[t];
+      dsc[db] = __float2half_rn(dd);
     } else {
       float dd = __fdiv_rn(amax, 127.0f);
       float id = dd != 0.0f ? __fdiv_rn(1.0f, dd) : 0.0f;
@@ -242,10 +267,10 @@ __global__ void k_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, in
         int q = (int)roundf(__fmul_rn(v[j], id));
         w[j / 4] |= (uint32_t)(uint8_t)(q + 128) << (8 * (j % 4));
       }
-      uint4 *o = reinterpret_cast<uint4 *>(qs) + 2 * b;
+      uint4 *o = reinterpret_cast<uint4 *>(qs + (r * dst_rs + dst_ro) * row_words) + 2 * cb;
       o[0] = make_uint4(w[0], w[1], w[2], w[3]);
       o[1] = make_uint4(w[4], w[5], w[6], w[7]);
-      dsc[b] = __float2half_rn(dd);
+      dsc[db] = __float2half_rn(dd);
     }
   }
 }
@@ -257,7 +282,7 @@ void launch_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, int64_t 
   FG_REQUIRE(dst.K == K && dst.qtype == qtype && (N - 1) * dst_rs + dst_ro < dst.N, FG_ERR_SHAPE,
              "synthetic quant: destination does not fit");
   int grid = (int)std::min<int64_t>(ceil_div(nb, 128), 148 * 16);
-  k_synth_quant<<<grid, 128, 0, s>>>(qtype, N, K, seed, row0, col0, k_full, stdv, dst_rs, dst_ro,
+  k_synth_quant<<<grid, 128, 0, s>>>(qtype, N, K, seed, row0, col0, k_full, stdv, dst_rs, dst_ro, dst.ldd, dst.row_words,
                                      const_cast<uint32_t *>(dst.qs), const_cast<__half *>(dst.d));
   FG_LAUNCH_CHECK();
 }

@@ -23,14 +23,20 @@ struct Tensor {
     return n;
   }
   QMat qmat() const {  // valid for FG_Q4_0 / FG_Q8_0 tensors of shape [N, K]
-    QMat q;
-    q.qtype = dtype;
-    q.N = shape[0];
-    q.K = shape[1];
-    q.qs = (const uint32_t *)ptr;
-    q.d = (const __half *)((const char *)ptr + qmat_d_offset(dtype, q.N, q.K));
-    return q;
+    return qmat_at(ptr, dtype, shape[0], shape[1]);
   }
+};
+
+// Workspace of the stream-K GEMV (gemv.cu): partial sums of row groups cut
+// between CTAs, arrival tickets (zero between launches) and the device error
+// word that bounded waits write on timeout.
+struct GemvScratch {
+  float *part = nullptr;
+  uint64_t part_floats = 0;
+  int *tickets = nullptr;
+  int64_t n_tickets = 0;
+  int *err = nullptr;
+  int maxc = 1;
 };
 
 // One context = one device, one stream, one handle namespace (the reference's
@@ -55,6 +61,7 @@ struct Ctx {
   cudaEvent_t staging_ev[2] = {nullptr, nullptr};
   uint64_t staging_bytes = 0;
   int num_sms = 148;
+  GemvScratch gemv;  // allocated at init, shared by every GEMV launch of the stream
 
   // allocation with quota accounting (quota.ts:65-313)
   void *alloc(uint64_t bytes);
@@ -66,6 +73,7 @@ struct Ctx {
   void h2d(void *dst, const void *src, uint64_t bytes);
   void d2h(void *dst, const void *src, uint64_t bytes);
   void sync();
+  void check_device_error();  // raises if a kernel's bounded wait timed out
 };
 
 uint64_t dtype_bytes(int dtype, int64_t numel, const int64_t *shape, int ndim);
@@ -105,13 +113,10 @@ struct Epilogue {
 };
 
 // gemv.cu: y = x W^T for up to 4 rows of x (the batch-1 decode path).
-// x [M][K] fp32; optional fused RMSNorm of x (gamma may be null).
+// x [M][ldx] fp32; optional fused RMSNorm of x (gamma may be null).
 bool gemv_supported(const QMat &w, int M);
-void launch_qgemv(const QMat &w, const float *x, int M, const float *norm_gamma, float norm_eps, bool do_norm,
-                  const Epilogue &ep, int num_sms, cudaStream_t s);
-// gemm.cu: the same contract for any M (prefill / batched decode).
 void launch_qgemv_ld(const QMat &w, const float *x, int M, int64_t ldx, const float *norm_gamma, float norm_eps,
-                     bool do_norm, const Epilogue &ep, int num_sms, cudaStream_t s);
+                     bool do_norm, const Epilogue &ep, const GemvScratch &sc, int num_sms, cudaStream_t s);
 // gemm.cu: the same contract without the fused norm, any M (prefill / batched decode).
 void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, int num_sms, cudaStream_t s);
 void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s);

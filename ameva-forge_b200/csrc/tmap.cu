@@ -1,0 +1,43 @@
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tmap.cuh"
+
+namespace fg {
+
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    cudaGetLastError();
+  });
+  FG_REQUIRE(fn != nullptr, FG_ERR_UNAVAILABLE, "cuTensorMapEncodeTiled is not available from the driver");
+  return fn;
+}
+}  // namespace
+
+CUtensorMap make_tmap_2d(const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows, uint64_t cols,
+                         uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols) {
+  FG_REQUIRE(((uintptr_t)base & 15) == 0 && pitch_bytes % 16 == 0 && (box_cols * elem_bytes) % 16 == 0 &&
+                 box_rows >= 1 && box_rows <= 256 && box_cols >= 1 && box_cols <= 256,
+             FG_ERR_VALIDATION, "tensor map: misaligned base/pitch/box");
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {pitch_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FG_REQUIRE(r == CUDA_SUCCESS, FG_ERR_INTERNAL_GPU, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return m;
+}
+
+}  // namespace fg

@@ -1,0 +1,34 @@
+// Host-side TMA tensor-map encoding (cuTensorMapEncodeTiled resolved through
+// the runtime's driver entry point, so the library does not link libcuda)
+// and the device-side tiled bulk-tensor load.
+#pragma once
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace fg {
+
+// 2-D row-major tensor [rows][cols] of `elem_bytes`-byte elements with a row
+// pitch of `pitch_bytes`, tiled in boxes of box_rows x box_cols elements; no
+// swizzle, out-of-bounds elements read as zero.  Requirements checked here:
+// base 16-byte aligned, pitch a multiple of 16, box_cols * elem_bytes a
+// multiple of 16.
+CUtensorMap make_tmap_2d(const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows, uint64_t cols,
+                         uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols);
+
+// Tiled 2-D load of the box at (x = column, y = row) into shared memory,
+// completing on `bar`.  x * elem_bytes must be a multiple of 16.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int32_t x, int32_t y, uint64_t *bar,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"((uint32_t)__cvta_generic_to_shared(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+}  // namespace fg

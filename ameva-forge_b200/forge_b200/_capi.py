@@ -11,7 +11,9 @@ import os
 from . import errors
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "_lib", "libforge_b200.so")
+# FORGE_B200_LIBRARY selects another build of the same library (profiling
+# experiments); by default the in-tree build is used.
+LIB_PATH = os.environ.get("FORGE_B200_LIBRARY") or os.path.join(_HERE, "_lib", "libforge_b200.so")
 
 FG_F32, FG_F16, FG_I32, FG_U8, FG_U32, FG_Q4_0, FG_Q8_0 = 0, 1, 3, 4, 5, 16, 17
 MAX_DIMS = 8
@@ -68,6 +70,7 @@ _SIGS = {
     "fg_unpack_quant": [c_vp, c_h, c_h, c_h, c_i32, c_i64, c_i64, P(c_h)],
     "fg_dequant": [c_vp, c_h, P(c_h)],
     "fg_qmatmul": [c_vp, c_h, c_h, P(c_h)],
+    "fg_qmatmul_into": [c_vp, c_h, c_h, c_h],
     "fg_matmul": [c_vp, c_h, c_h, P(c_h)],
     "fg_flash_attention": [c_vp, c_h, c_h, c_h, c_f32, c_i32, c_i32, P(c_h)],
     "fg_rmsnorm": [c_vp, c_h, c_h, c_f32, P(c_h)],

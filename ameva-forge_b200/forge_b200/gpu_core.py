@@ -165,6 +165,15 @@ class Context:
     def qmatmul(self, x, w) -> str:
         return self._op("fg_qmatmul", _h(x), _h(w))
 
+    def qmatmul_into(self, x, w, out) -> str:
+        C.call("fg_qmatmul_into", self.ptr, _h(x), _h(w), _h(out))
+        return out
+
+    def stream_ptr(self) -> int:
+        s = ctypes.c_void_p()
+        C.call("fg_get_stream", self.ptr, ctypes.byref(s))
+        return s.value
+
     def matmul(self, a, b) -> str:
         return self._op("fg_matmul", _h(a), _h(b))
 

@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="forge_b200", choices=["forge_b200", "reference"])
     ap.add_argument("--cpu-baseline", type=int, default=1, help="time the CPU oracle sample (rank 0, N=1)")
+    ap.add_argument("--roofline-only", action="store_true",
+                    help="only time the dequant-GEMV on the layer shapes (the profiling case)")
     return ap.parse_args()
 
 
@@ -173,49 +175,48 @@ def run_reference(args, rank, world):
 
 
 # ------------------------------------------------------------------ roofline
-def gemv_roofline(ctx, world, reps=8):
+def gemv_roofline(ctx, world, reps=8, rounds=10):
     """Time the fused dequant-GEMV alone on this rank's 7B shard shapes with
-    cold L2 (rotating over `reps` weight copies of each shape, > 2x L2)."""
-    import forge_b200  # noqa: F401
-    H, I, V, d = 4096, 11008, 32000, 128
+    cold L2 (each replay rotates over `reps` distinct weight copies per shape,
+    > 2x L2).  The launches are captured in a CUDA graph on the library's
+    stream (fg_qmatmul_into allocates nothing), so the events measure device
+    time only.  Returns (algorithmic bytes per launch, ms per launch, detail)."""
+    H, I, d = 4096, 11008, 128
     shapes = [((3 * 32 // world) * d, H), (H, 32 // world * d), (2 * I // world, H), (H, I // world)]
-    ws, xs = [], {}
+    stream = torch.cuda.ExternalStream(ctx.stream_ptr())
+    total_bytes, total_ms, launches, per_shape = 0, 0.0, 0, []
     for si, (N, K) in enumerate(shapes):
-        for r in range(reps):
-            ws.append((ctx.synth_quant("Q4_0", N, K, seed=1000 * si + r, std=0.02), N, K))
-        xs[K] = ctx.synth_normal((1, K), np.float32, seed=K)
-    stream = torch.cuda.ExternalStream(ctx_stream(ctx))
-    outs = []
-    for h, N, K in ws[:4]:  # warm up every instantiation
-        outs.append(ctx.qmatmul(xs[K], h))
-    ctx.synchronize()
-    for o in outs:
-        ctx.dispose(o)
-    total_bytes, total_ms, launches = 0, 0.0, 0
-    per_shape = []
-    for si in range(len(shapes)):
-        group = [w for w in ws if (w[1], w[2]) == shapes[si]]
-        N, K = shapes[si]
+        ws = [ctx.synth_quant("Q4_0", N, K, seed=1000 * si + r, std=0.02) for r in range(reps)]
+        x = ctx.synth_normal((1, K), np.float32, seed=K)
+        out = ctx.empty((1, N), np.float32)
+        for w in ws:  # warm-up outside capture (sets kernel attributes)
+            ctx.qmatmul_into(x, w, out)
+        ctx.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for w in ws:
+                ctx.qmatmul_into(x, w, out)
         with torch.cuda.stream(stream):
+            g.replay()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            outs = [ctx.qmatmul(xs[K], h) for h, _, _ in group]
+            for _ in range(rounds):
+                g.replay()
             e1.record()
         e1.synchronize()
         ms = e0.elapsed_time(e1)
-        b = len(group) * (N * K // 32 * 18 + 4 * (K + N))
-        per_shape.append({"N": N, "K": K, "us_per_launch": 1000 * ms / len(group),
-                          "GBps": b / (ms / 1e3) / 1e9})
+        n = rounds * reps
+        b = n * (N * K // 32 * 18 + 4 * (K + N))
+        per_shape.append({"N": N, "K": K, "us_per_launch": 1000 * ms / n, "GBps": b / (ms / 1e3) / 1e9})
         total_bytes += b
         total_ms += ms
-        launches += len(group)
-        for o in outs:
-            ctx.dispose(o)
-    for h, _, _ in ws:
-        ctx.dispose(h)
-    for x in xs.values():
+        launches += n
+        del g
+        for w in ws:
+            ctx.dispose(w)
         ctx.dispose(x)
-    ctx.synchronize()
+        ctx.dispose(out)
+        ctx.synchronize()
     return total_bytes / launches, total_ms / launches, per_shape
 
 
@@ -260,6 +261,14 @@ def main():
         return
 
     import forge_b200
+    if args.roofline_only:
+        ctx = forge_b200.Context(device=local)
+        b_launch, ms_launch, per_shape = gemv_roofline(ctx, world)
+        peak, _ = measured_peak()
+        print(json.dumps({"kernel": "k_qgemv", "GBps": b_launch / (ms_launch / 1e3) / 1e9, "peak": peak,
+                          "per_shape": per_shape}), flush=True)
+        ctx.shutdown()
+        return
     nid = None
     if world > 1:
         obj = [forge_b200.nccl_unique_id() if rank == 0 else None]

@@ -159,6 +159,10 @@ int fg_dequant(fg_ctx *ctx, fg_handle w, fg_handle *out);
  * W a Q4_0/Q8_0 [N, K] tensor, fp32 accumulation.  Dequantisation is fused
  * into the GEMV (up to 4 rows of x) or GEMM that consumes it. */
 int fg_qmatmul(fg_ctx *ctx, fg_handle x, fg_handle w, fg_handle *out);
+/* fg_qmatmul into an existing F32 tensor `out` of x's shape with the last
+ * dimension N (no allocation, so a caller can capture it in a CUDA graph on
+ * the context stream). */
+int fg_qmatmul_into(fg_ctx *ctx, fg_handle x, fg_handle w, fg_handle out);
 /* gpuCore.matmul (gpuCore.ts:713-761): C[M,N] = A[M,K] B[K,N], fp32. */
 int fg_matmul(fg_ctx *ctx, fg_handle a, fg_handle b, fg_handle *out);
 /* gpuCore.flashAttention (gpuCore.ts:949-1017): Q [B,H,Nq,d], K/V
