@@ -73,6 +73,7 @@ _SIGS = {
     "fg_qmatmul_into": [c_vp, c_h, c_h, c_h],
     "fg_matmul": [c_vp, c_h, c_h, P(c_h)],
     "fg_flash_attention": [c_vp, c_h, c_h, c_h, c_f32, c_i32, c_i32, P(c_h)],
+    "fg_attention_decode_static": [c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_i32, c_i32, c_i64, c_i32, c_f32, c_vp],
     "fg_rmsnorm": [c_vp, c_h, c_h, c_f32, P(c_h)],
     "fg_rope": [c_vp, c_h, c_f32, c_i64, P(c_h)],
     "fg_swiglu": [c_vp, c_h, c_h, P(c_h)],

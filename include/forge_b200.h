@@ -171,6 +171,23 @@ int fg_matmul(fg_ctx *ctx, fg_handle a, fg_handle b, fg_handle *out);
  * (fp32 softmax statistics).  Output dtype = F32. */
 int fg_flash_attention(fg_ctx *ctx, fg_handle q, fg_handle k, fg_handle v, float scale,
                        int32_t has_scale, int32_t causal, fg_handle *out);
+/* Decode attention (one query token per sequence) that allocates nothing.
+ * No counterpart in the reference: it serves hosts that cannot allocate at
+ * call time (device memory fully committed to their own KV cache under a hard
+ * quota, latency-critical threads where cudaMalloc/cudaFree would synchronise
+ * the device, hosts without an fg_ctx).  Raw device pointers: q and out F32
+ * [batch, heads, head_dim]; k_cache and v_cache F16 [batch, kv_heads,
+ * cache_capacity, head_dim], of which the first n_kv positions are attended.
+ * head_dim 64 or 128, heads / kv_heads in {1, 2, 4, 8}.  Runs on `stream`
+ * (a cudaStream_t; NULL = legacy default stream) of the current device.
+ * Split-KV scratch comes from a 2 MiB static device array: shapes that need
+ * more return FG_ERR_VALIDATION.  Calls on one device must not overlap in
+ * time (they share the array); calls queued on one stream are safe.  The
+ * first call on each device looks up the array's address and must not be
+ * made during stream capture. */
+int fg_attention_decode_static(const float *q, const void *k_cache, const void *v_cache, float *out,
+                               int32_t batch, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                               int64_t cache_capacity, int32_t n_kv, float scale, void *stream);
 /* gpuCore.rmsNorm (rmsnorm.wgsl.ts:10-74); gamma 0 = none. */
 int fg_rmsnorm(fg_ctx *ctx, fg_handle x, fg_handle gamma, float eps, fg_handle *out);
 /* gpuCore.rope (rope.wgsl.ts:11-62): interleaved pairs, x [B,H,N,d]. */
