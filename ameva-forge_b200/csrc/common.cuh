@@ -98,40 +98,65 @@ __device__ inline float normal01(uint64_t seed, uint64_t i) {
 }
 
 // ---------------------------------------------------------------- quant layout
-// A quantized [N, K] matrix lives in one allocation:
-//   qs : Q8_0 -- the reference unpack packing (unpack_quant.wgsl.ts:44-51):
-//        byte i%4 of u32 word i/4 holds q + 128 for element i of the row;
-//        Q4_0 -- codes (q + 8) regrouped for the tensor-core GEMV fragments:
-//        a row holds its blocks rounded up to a multiple of 4 (zero padded);
-//        the 4 words of block b sit at word (b/4)*16 + t*4 + b%4, and word t
-//        holds, in nibbles 0..7, the codes of block elements
-//        2t, 2t+8, 16+2t, 24+2t, 2t+1, 2t+9, 17+2t, 25+2t (q4_elem);
-//   d  : fp16 scale per 32-element block, [N][ldd], 256-byte aligned; rows
-//        padded to a multiple of 8 scales (16 bytes) for the TMA row pitch.
+// A quantized [N, K] matrix lives in one allocation.
+//
+// Q8_0 -- qs: the reference unpack packing (unpack_quant.wgsl.ts:44-51), byte
+//   i%4 of u32 word i/4 of a row holds q + 128 for element i; d: fp16 scale
+//   per 32-element block, [N][ldd] after qs (256-byte aligned), rows padded to
+//   a multiple of 8 scales (16 bytes) for the TMA row pitch.
+//
+// Q4_0 -- tiles of 128 rows x 8 blocks (18,432 bytes each), so that the GEMV
+//   streams each tile with one contiguous bulk copy.  Tile (g, c) holds rows
+//   128g.. and blocks 8c..; tiles are stored row-group major ([g][c]), rows
+//   and blocks past N and K/32 are zero.  Inside a tile:
+//     bytes [0, 16384): codes (q + 8), 128 bytes per row: the 16 words of
+//       block quad j (blocks 4j..4j+3) sit at 64-byte half (j ^ (row & 1)) of
+//       the row (the swap puts neighbouring rows on different shared-memory
+//       banks); in a half, lane-word t of block 4j+i is word t*4 + i.  Word t
+//       of a block is GGUF bytes 4t..4t+3 of its qs: the low nibble of byte
+//       i holds element 4t + i and the high nibble element 16 + 4t + i
+//       (q4_elem) -- the k order of the int8 A fragments of mma.sync
+//       m16n8k32 (a0/a1: k = 4t..4t+3, a2/a3: k = 16+4t..16+4t+3), so a
+//       mask (and a shift) turns a word into two fragment registers;
+//     bytes [16384, 18432): fp16 scales, [128 rows][8 blocks].
+constexpr int kQ4TileRows = 128, kQ4TileBlocks = 8;
+constexpr int kQ4TileCodeBytes = kQ4TileRows * kQ4TileBlocks * 16;
+constexpr int kQ4TileBytes = kQ4TileCodeBytes + kQ4TileRows * kQ4TileBlocks * 2;
 struct QMat {
   const uint32_t *qs;
-  const __half *d;
-  int32_t qtype;  // FG_Q4_0 / FG_Q8_0
+  const __half *d;    // Q4_0: the allocation base (scales sit inside the tiles)
+  int32_t qtype;      // FG_Q4_0 / FG_Q8_0
   int64_t N, K;
-  int64_t ldd;        // scales per d row (K/32 rounded up to 8)
-  int64_t row_words;  // u32 words per qs row
+  int64_t ldd;        // Q8_0: scales per d row (K/32 rounded up to 8)
+  int64_t row_words;  // Q8_0: u32 words per qs row; Q4_0: tiles per row group
 };
 __host__ __device__ inline int64_t qmat_ldd(int64_t K) { return (K / 32 + 7) / 8 * 8; }
+__host__ __device__ inline int64_t q4_chunks(int64_t K) { return (K / 32 + kQ4TileBlocks - 1) / kQ4TileBlocks; }
+__host__ __device__ inline int64_t q4_groups(int64_t N) { return (N + kQ4TileRows - 1) / kQ4TileRows; }
 __host__ __device__ inline int64_t qmat_row_words(int qtype, int64_t K) {
-  return qtype == FG_Q4_0 ? (K / 32 + 3) / 4 * 16 : K / 4;
+  return qtype == FG_Q4_0 ? q4_chunks(K) : K / 4;
 }
-// Block element held by nibble p of word t (Q4_0 device packing).
-__host__ __device__ inline int q4_elem(int t, int p) {
-  const int base = (p & 3) == 0 ? 0 : (p & 3) == 1 ? 8 : (p & 3) == 2 ? 16 : 24;
-  return base + 2 * t + (p >> 2);
+// Block element held by nibble p of lane-word t (Q4_0 device packing).
+__host__ __device__ inline int q4_elem(int t, int p) { return 4 * t + (p >> 1) + 16 * (p & 1); }
+// Q4_0: u32 index (from qs) of lane-word t of block b of row n.
+__host__ __device__ inline int64_t q4_word_at(const QMat &w, int64_t n, int64_t b, int t) {
+  const int64_t tile = (n / kQ4TileRows) * w.row_words + b / kQ4TileBlocks;
+  const int r = (int)(n % kQ4TileRows), bb = (int)(b % kQ4TileBlocks);
+  return tile * (kQ4TileBytes / 4) + r * 32 + (((bb >> 2) ^ (r & 1)) << 4) + t * 4 + (bb & 3);
 }
-// Word (within the row) holding lane-word t of block b (Q4_0 device packing).
-__host__ __device__ inline int64_t q4_word(int64_t b, int t) { return (b >> 2) * 16 + t * 4 + (b & 3); }
+// fp16 scale index (from d) of block b of row n, both layouts.
+__host__ __device__ inline int64_t qmat_scale_at(const QMat &w, int64_t n, int64_t b) {
+  if (w.qtype != FG_Q4_0) return n * w.ldd + b;
+  const int64_t tile = (n / kQ4TileRows) * w.row_words + b / kQ4TileBlocks;
+  return tile * (kQ4TileBytes / 2) + kQ4TileCodeBytes / 2 + (n % kQ4TileRows) * kQ4TileBlocks + b % kQ4TileBlocks;
+}
 inline uint64_t qmat_qs_bytes(int qtype, int64_t N, int64_t K) {
+  if (qtype == FG_Q4_0) return (uint64_t)q4_groups(N) * (uint64_t)q4_chunks(K) * kQ4TileBytes;
   return (uint64_t)N * (uint64_t)qmat_row_words(qtype, K) * 4;
 }
 inline uint64_t qmat_d_offset(int qtype, int64_t N, int64_t K) { return align_up(qmat_qs_bytes(qtype, N, K), 256); }
 inline uint64_t qmat_bytes(int qtype, int64_t N, int64_t K) {
+  if (qtype == FG_Q4_0) return qmat_qs_bytes(qtype, N, K);
   return qmat_d_offset(qtype, N, K) + (uint64_t)N * (uint64_t)qmat_ldd(K) * 2;
 }
 inline QMat qmat_at(void *base, int qtype, int64_t N, int64_t K) {
@@ -139,10 +164,10 @@ inline QMat qmat_at(void *base, int qtype, int64_t N, int64_t K) {
   q.qtype = qtype;
   q.N = N;
   q.K = K;
-  q.ldd = qmat_ldd(K);
+  q.ldd = qtype == FG_Q4_0 ? 0 : qmat_ldd(K);
   q.row_words = qmat_row_words(qtype, K);
   q.qs = (const uint32_t *)base;
-  q.d = (const __half *)((const char *)base + qmat_d_offset(qtype, N, K));
+  q.d = qtype == FG_Q4_0 ? (const __half *)base : (const __half *)((const char *)base + qmat_d_offset(qtype, N, K));
   return q;
 }
 inline int gguf_block_bytes(int qtype) { return qtype == FG_Q4_0 ? 18 : 34; }

@@ -46,9 +46,9 @@ __global__ void __launch_bounds__(256) k_qgemm_simt(QMat w, const float *__restr
     {
       const int r = tid >> 2, t = tid & 3;
       const int64_t n = n0 + r;
-      const float sc = n < w.N ? __half2float(w.d[n * w.ldd + kb]) : 0.0f;
+      const float sc = n < w.N ? __half2float(w.d[qmat_scale_at(w, n, kb)]) : 0.0f;
       if (w.qtype == FG_Q4_0) {
-        const uint32_t word = n < w.N ? w.qs[n * w.row_words + q4_word(kb, t)] : 0x88888888u;
+        const uint32_t word = n < w.N ? w.qs[q4_word_at(w, n, kb, t)] : 0x88888888u;
 #pragma unroll
         for (int p = 0; p < 8; ++p)
           ws[q4_elem(t, p)][r] = __fmul_rn(__fsub_rn((float)((word >> (4 * p)) & 0xFu), 8.0f), sc);

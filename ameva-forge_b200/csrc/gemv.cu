@@ -5,37 +5,30 @@
 // (18 B Q4_0 | 34 B Q8_0) + 4*M*(K + N); every weight byte is read once.
 //
 // Shared structure (sm_100a):
-//  * two CTAs per SM, each a producer thread plus 8 consumer warps: the
-//    producer streams weight tiles (Q4_0: 128 rows x 128 code bytes, Q8_0: 32
-//    rows x 512, plus their fp16 scales) with two 2-D TMA loads
-//    (cp.async.bulk.tensor, out-of-range rows zero-filled by the TMA unit)
-//    into a 3-stage shared-memory ring tracked by mbarriers (~100 KB per SM in
-//    flight).  The kernel releases its dependents at start (programmatic
-//    dependent launch), so the next kernel's CTAs fill the SM slots freed by
-//    this kernel's retiring CTAs and begin streaming their own weights --
-//    which do not depend on this kernel -- during its tail;
+//  * a producer thread plus 8 consumer warps per CTA, two CTAs per SM (one
+//    when the staged x needs more shared memory).  The producer streams the
+//    weights into a shared-memory ring tracked by mbarriers: Q4_0 one
+//    contiguous 18 KB tile (128 rows x 8 blocks with their scales, the
+//    device layout of common.cuh) per stage with a 1-D bulk copy
+//    (cp.async.bulk), 4 stages; Q8_0 32 rows x 512 code bytes plus scales
+//    with two 2-D tensor-map loads (cp.async.bulk.tensor), 3 stages.  The
+//    kernel releases its dependents at start (programmatic dependent
+//    launch), so the next kernel's CTAs fill the SM slots freed by this
+//    kernel's retiring CTAs and begin streaming their own weights -- which do
+//    not depend on this kernel -- during its tail;
 //  * (row-group, chunk) work units are split evenly over the CTAs
-//    (stream-K): a row group cut between CTAs is finished by the last CTA
-//    to arrive (atomic ticket), which sums the partials in CTA order, so
-//    results are deterministic and every fused epilogue sees complete sums;
+//    (stream-K): a CTA's units are consecutive tiles, i.e. one contiguous
+//    range of the matrix.  A row group cut between CTAs is finished by the
+//    last CTA to arrive (atomic ticket), which sums the partials in CTA
+//    order, so results are deterministic and every fused epilogue sees
+//    complete sums;
 //  * the x vector(s) are staged once per CTA in shared memory with the
 //    RMSNorm that precedes every projection fused in.
 //
-// Q4_0 math (k_qgemv_q4): tensor cores do the multiply-add.  One LOP3 turns
-// two 4-bit codes into the fp16 pair (1024 + n, 1024 + n') -- or (1024 + 16n,
-// ...) for the codes stored at nibble offsets 4 -- which mma.sync m16n8k16
-// multiplies by x with fp32 accumulation.  x enters as a pair of fp16 columns
-// (hi, lo = x - hi) per token, i.e. with ~22 significant bits, after a
-// power-of-two range scaling; the 16x weight scale of half the codes is
-// folded into x, and the 1024 offset and the -8 zero point are removed
-// exactly by a per-block correction sum(x) * (1024 + 8 s) fed in as the MMA
-// accumulator input.  Each block's fp32 result is scaled by its fp16 d.  The
-// codes are stored in fragment order at upload (q4_elem), so every lane
-// loads one u32 per row and block and spends 5 integer ops per 8 weights.
-//
-// Q8_0 math (k_qgemv_q8): CUDA cores.  PRMT places a byte into the mantissa
-// of 2^23 (0x4B000000 | byte); one packed FADD2 removes 2^23 + 128 exactly and
-// packed FFMA2 accumulates in fp32, scaled by d once per block.
+// Q4_0 math (k_qgemv_q4): integer tensor-core MMA, see the comment above the
+// kernel.  Q8_0 math (k_qgemv_q8): CUDA cores.  PRMT places a byte into the
+// mantissa of 2^23 (0x4B000000 | byte); one packed FADD2 removes 2^23 + 128
+// exactly and packed FFMA2 accumulates in fp32, scaled by d once per block.
 #include "epilogue.cuh"
 #include "tma.cuh"
 #include "tmap.cuh"
@@ -51,6 +44,7 @@ constexpr int kTileBytes = 512;  // code bytes per row per chunk (one TMA box wi
 constexpr int kStages = 3;
 
 __device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // CTA that owns work unit u when U units are split evenly over P CTAs
@@ -81,7 +75,28 @@ __device__ __forceinline__ Sched schedule(const QMat &w, int nb_chunked) {
   return s;
 }
 
-// Producer thread: stream the units [u0, u1) through the ring.
+// Producer thread, Q4_0: unit u is tile u of the tiled layout (common.cuh),
+// one contiguous bulk copy; a CTA's units are consecutive tiles, so each CTA
+// streams one contiguous range of the matrix.
+template <int STAGES>
+__device__ __forceinline__ void produce_tiles(const unsigned char *tiles, const Sched &sc, unsigned char *ring,
+                                              uint64_t *full, uint64_t *empty, int *err) {
+  const uint64_t pol = l2_evict_first_policy();
+  int i = 0;
+  for (int u = sc.u0; u < sc.u1; ++u, ++i) {
+    const int s = i % STAGES;
+    const uint32_t k = (uint32_t)(i / STAGES);
+    if (i >= STAGES && !mbar_wait(&empty[s], (k - 1) & 1, err, DEVERR_GEMV_EMPTY)) break;
+    mbar_arrive_expect_tx(&full[s], kQ4TileBytes);
+    bulk_g2s(ring + s * kQ4TileBytes, tiles + (int64_t)u * kQ4TileBytes, kQ4TileBytes, &full[s], pol);
+  }
+  // drain: no copy may still be landing in this CTA's shared memory on exit
+  for (int j = i > STAGES ? i - STAGES : 0; j < i; ++j)
+    mbar_wait(&full[j % STAGES], (uint32_t)(j / STAGES) & 1, err, DEVERR_DRAIN);
+}
+
+// Producer thread, Q8_0: stream the units [u0, u1) through the ring with 2-D
+// tensor-map loads of the codes and scales.
 template <int ROWS, int TB, int CB>
 __device__ __forceinline__ void produce(const CUtensorMap *tq, const CUtensorMap *td, const Sched &sc,
                                         unsigned char *ring, uint64_t *full, uint64_t *empty, int *err) {
@@ -112,7 +127,8 @@ __device__ __forceinline__ void produce(const CUtensorMap *tq, const CUtensorMap
 // reduced over this CTA's warps): epilogue directly, or stream-K fix-up.
 template <int ROWS, int MV>
 __device__ __forceinline__ void finish_group(const QMat &w, const Epilogue &ep, const GemvScratch &scr,
-                                             const Sched &sc, int g, const float *red, int *s_last, bool ok) {
+                                             const Sched &sc, int g, const float *red, const float *mul, int *s_last,
+                                             bool ok) {
   constexpr int kRows = ROWS;
   const int tid = threadIdx.x;
   const int first = g * sc.nc, last = first + sc.nc - 1;
@@ -147,6 +163,10 @@ __device__ __forceinline__ void finish_group(const QMat &w, const Epilogue &ep, 
         v1 += __ldcg(pg + jj * kRows * MV + (2 * p + 1) * MV + m);
       }
     }
+    if (mul) {
+      v0 *= mul[m];
+      v1 *= mul[m];
+    }
     const int64_t n = (int64_t)g * kRows + 2 * p;
     if (n + 1 < w.N)
       epi_store_pair(ep, n, m, v0, v1);
@@ -156,50 +176,66 @@ __device__ __forceinline__ void finish_group(const QMat &w, const Epilogue &ep, 
 }
 
 // ---------------------------------------------------------------------------
-// Q4_0 tensor-core GEMV: 128-row groups; warp w owns rows 16w..16w+15 of the
-// group for the whole K sweep (no cross-warp reduction); a stage is 128 rows
-// x 8 blocks (two quads), one m16n8k16 pair per block.
+// Q4_0 tensor-core GEMV (integer MMA).  128-row groups; warp w owns rows
+// 16w..16w+15 of the group for the whole K sweep (no cross-warp reduction); a
+// stage is one tile (128 rows x 8 blocks), one mma.sync m16n8k32 per block
+// and 16 rows: A = the u8 codes (q + 8, straight from the GGUF bytes), B = two
+// s8 digit columns per token, D = exact int32 dot products.
+//
+// x staging: every 32-element block of x' (x, times gamma when the RMSNorm is
+// fused) gets a power-of-two scale 2^e with max|x'| 2^e in [2^20, 2^21);
+// v = rn(x' 2^e) (22 bits) splits into digits hi = v >> 14 in [-128, 127],
+// mid = (v >> 7) & 127 and lo = v & 127.  A token takes four B columns (hi,
+// mid, lo, 0), so one MMA serves two tokens; the lanes of D columns (hi, mid)
+// accumulate 128 D_hi + D_mid, those of (lo, 0) accumulate 128 D_lo, and the
+// two combine exactly at the end as 128 a + b / 128.  The MMA accumulator
+// input is -8 * (sum of the block's digits), which removes the code offset
+// exactly, so D = sum (q - 8) * digit, and per block and row the kernel adds
+// d * 2^-e * D' into an fp32 accumulator.  Scales are local to a block, so
+// one large activation does not coarsen the others.  The RMSNorm's 1/rms
+// multiplies the finished sums.
 // ---------------------------------------------------------------------------
-constexpr int kQ4Rows = 128, kQ4TB = 128, kQ4CB = 8;
+constexpr int kQ4Rows = kQ4TileRows, kQ4TB = 128, kQ4CB = kQ4TileBlocks;
+constexpr int kQ4Stages = 4;
 using GeoQ4 = Geo<kQ4Rows, kQ4TB, kQ4CB>;
+static_assert(GeoQ4::SB == kQ4TileBytes && GeoQ4::SQ == kQ4TileCodeBytes, "stage = one Q4_0 tile");
 
-__device__ __forceinline__ void mma_f16_zc(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%10,%10,%10};"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+__device__ __forceinline__ void imma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                          uint32_t b1, int c0, int c1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
 }
-__device__ __forceinline__ void mma_f16(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+
+// Digits of 4 consecutive elements packed as s8 bytes.
+__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
+  return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) | ((uint32_t)d << 24);
 }
 
 template <int MV>
 __global__ void __launch_bounds__(kThreads, 2)
-    k_qgemv_q4(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap td, QMat w,
-               const float *__restrict__ x, int64_t ldx, const float *__restrict__ gamma, float eps, int do_norm,
+    k_qgemv_q4(QMat w, const float *__restrict__ x, int64_t ldx, const float *__restrict__ gamma, float eps, int do_norm,
                Epilogue ep, GemvScratch scr) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char *ring = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages];
-  __shared__ float s_sum[kConsumers][MV], s_max[kConsumers][MV], s_gmax[kConsumers];
-  __shared__ float s_mul[MV], s_sigma[MV], s_inv_sigma[MV];
+  __shared__ __align__(8) uint64_t full[kQ4Stages], empty[kQ4Stages];
+  __shared__ float s_sum[kConsumers][MV];
+  __shared__ float s_inv[MV];
   __shared__ int s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nb = (int)(w.K >> 5);
   const Sched sc = schedule<kQ4Rows>(w, (nb + kQ4CB - 1) / kQ4CB);
   const int nbx = sc.nc * kQ4CB;  // blocks staged (zero past nb)
-  uint4 *xf = reinterpret_cast<uint4 *>(ring + kStages * GeoQ4::SB);  // [nbx][2MV][4] fp16 fragments
-  float *corr = reinterpret_cast<float *>(xf + nbx * 2 * MV * 4);      // [MV][nbx] negated corrections
-  float *red = corr + MV * nbx;                                        // [256][MV]
+  constexpr int NM = (MV + 1) / 2;  // MMAs per block: two tokens each
+  uint2 *xb = reinterpret_cast<uint2 *>(ring + kQ4Stages * GeoQ4::SB);  // [nbx][3 MV digit cols][4 t]
+  int *cx0 = reinterpret_cast<int *>(xb + nbx * 3 * MV * 4);            // [2 MV][nbx] MMA C, col 2t
+  int *cx1 = cx0 + 2 * MV * nbx;                                        // [2 MV][nbx] MMA C, col 2t+1
+  float *fbk = reinterpret_cast<float *>(cx1 + 2 * MV * nbx);           // [MV][nbx] 2^-e
+  float *red = fbk + MV * nbx;                                          // [128][MV]
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kQ4Stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
     }
@@ -211,153 +247,148 @@ __global__ void __launch_bounds__(kThreads, 2)
   // kernel finishes (they wait for this kernel's results before reading x).
   asm volatile("griddepcontrol.launch_dependents;");
   if (warp == kConsumers) {
-    if (lane == 0) produce<kQ4Rows, kQ4TB, kQ4CB>(&tq, &td, sc, ring, full, empty, scr.err);
+    if (lane == 0)
+      produce_tiles<kQ4Stages>(reinterpret_cast<const unsigned char *>(w.qs), sc, ring, full, empty, scr.err);
     return;
   }
 
   // ---------------- stage x (after the producer of x has finished)
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  const int K = (int)w.K;
-  {  // statistics: sum of squares (RMSNorm), max |x|, max |gamma|
-    float ss[MV], mx[MV], gm = 0.0f;
-#pragma unroll
-    for (int m = 0; m < MV; ++m) ss[m] = mx[m] = 0.0f;
-    for (int i = tid; i < K / 4; i += kCThreads) {
-#pragma unroll
-      for (int m = 0; m < MV; ++m) {
-        const float4 v = *reinterpret_cast<const float4 *>(x + m * ldx + 4 * i);
-        ss[m] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-        mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-      }
-      if (do_norm && gamma) {
-        const float4 gv = *reinterpret_cast<const float4 *>(gamma + 4 * i);
-        gm = fmaxf(gm, fmaxf(fmaxf(fabsf(gv.x), fabsf(gv.y)), fmaxf(fabsf(gv.z), fabsf(gv.w))));
-      }
-    }
+  {
+    const int q = lane & 7;  // 4-element group of the block; 8 lanes per block
 #pragma unroll
     for (int m = 0; m < MV; ++m) {
-      const float s = warp_sum(ss[m]), a = warp_max(mx[m]);
-      if (lane == 0) {
-        s_sum[warp][m] = s;
-        s_max[warp][m] = a;
-      }
-    }
-    gm = warp_max(gm);
-    if (lane == 0) s_gmax[warp] = gm;
-    named_sync(kCThreads);
-    if (tid < MV) {
-      float s = 0.0f, a = 0.0f, gmax = 0.0f;
-      for (int i = 0; i < kConsumers; ++i) {
-        s += s_sum[i][tid];
-        a = fmaxf(a, s_max[i][tid]);
-        gmax = fmaxf(gmax, s_gmax[i]);
-      }
-      float inv = 1.0f, bound = a;
-      if (do_norm) {
-        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)K), eps)));
-        bound = a * inv * (gamma ? gmax : 1.0f);
-      }
-      // power-of-two range scaling: max |x * sigma| < 2^14 in fp16
-      int e = 0;
-      if (bound > 0.0f && bound < INFINITY) frexpf(bound, &e);
-      e = min(max(14 - e, -100), 100);
-      s_mul[tid] = inv;
-      s_sigma[tid] = ldexpf(1.0f, e);
-      s_inv_sigma[tid] = ldexpf(1.0f, -e);
-    }
-    named_sync(kCThreads);
-  }
-  for (int item = tid; item < MV * nbx * 4; item += kCThreads) {
-    const int t = item & 3;
-    const int bb = (item >> 2) % nbx;
-    const int m = (item >> 2) / nbx;
-    const float inv = s_mul[m], sigma = s_sigma[m];
-    uint32_t hi[4], lo[4];
-    float csum = 0.0f;
-#pragma unroll
-    for (int f = 0; f < 4; ++f) {
-      // fragment f of lane-word t: elements (2t, 2t+1) + {0, 8, 16, 24}[f]
-      float2 v = make_float2(0.0f, 0.0f);
-      if (bb < nb) {
-        const int k = bb * 32 + 2 * t + 8 * f;
-        v = *reinterpret_cast<const float2 *>(x + m * ldx + k);
-        if (do_norm) {
-          v.x = __fmul_rn(v.x, inv);
-          v.y = __fmul_rn(v.y, inv);
-          if (gamma) {
-            const float2 gv = *reinterpret_cast<const float2 *>(gamma + k);
-            v.x = __fmul_rn(v.x, gv.x);
-            v.y = __fmul_rn(v.y, gv.y);
+      float ss = 0.0f;
+      for (int item = tid; item < nbx * 8; item += kCThreads) {
+        const int bb = item >> 3;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (bb < nb) {
+          const int k = bb * 32 + 4 * q;
+          v = *reinterpret_cast<const float4 *>(x + m * ldx + k);
+          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+          if (do_norm && gamma) {
+            const float4 g = *reinterpret_cast<const float4 *>(gamma + k);
+            v.x *= g.x;
+            v.y *= g.y;
+            v.z *= g.z;
+            v.w *= g.w;
           }
         }
+        float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        // amax in [2^E, 2^(E+1)) -> scale 2^(20 - E); zero / subnormal blocks keep 2^126 (digits ~0)
+        const int E = ((__float_as_int(amax) >> 23) & 0xFF) - 127;
+        const int e = min(max(20 - E, -126), 126);
+        const float scl = __int_as_float((e + 127) << 23);
+        const float vf[4] = {v.x, v.y, v.z, v.w};
+        int hi[4], mi[4], lo[4], shi = 0, smi = 0, slo = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int vi = __float2int_rn(fminf(fmaxf(vf[i] * scl, -2097152.0f), 2097151.0f));
+          hi[i] = vi >> 14;
+          mi[i] = (vi >> 7) & 127;
+          lo[i] = vi & 127;
+          shi += hi[i];
+          smi += mi[i];
+          slo += lo[i];
+        }
+        {
+          // B fragment words of digit columns 3m, 3m+1, 3m+2: lane-word t = q & 3, half q >> 2
+          uint32_t *col = reinterpret_cast<uint32_t *>(xb + (bb * 3 * MV + 3 * m) * 4) + (q & 3) * 2 + (q >> 2);
+          col[0] = pack_s8x4(hi[0], hi[1], hi[2], hi[3]);
+          col[8] = pack_s8x4(mi[0], mi[1], mi[2], mi[3]);
+          col[16] = pack_s8x4(lo[0], lo[1], lo[2], lo[3]);
+        }
+#pragma unroll
+        for (int o = 1; o < 8; o <<= 1) {
+          shi += __shfl_xor_sync(0xffffffffu, shi, o);
+          smi += __shfl_xor_sync(0xffffffffu, smi, o);
+          slo += __shfl_xor_sync(0xffffffffu, slo, o);
+        }
+        if (q == 0) {
+          // C of the lanes holding (hi, mid) and (lo, 0) of token m
+          cx0[(2 * m) * nbx + bb] = -8 * shi;
+          cx1[(2 * m) * nbx + bb] = -8 * smi;
+          cx0[(2 * m + 1) * nbx + bb] = -8 * slo;
+          cx1[(2 * m + 1) * nbx + bb] = 0;
+          // non-finite inputs make the block factor NaN, so the outputs are NaN
+          fbk[m * nbx + bb] = amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000);
+        }
       }
-      const float sf = (f & 1) ? 0.0625f * sigma : sigma;  // logical k >= 8 of a half: codes carry x16
-      v.x *= sf;
-      v.y *= sf;
-      const __half2 h = __floats2half2_rn(v.x, v.y);
-      const float2 hf = __half22float2(h);
-      const __half2 l = __floats2half2_rn(v.x - hf.x, v.y - hf.y);
-      const float2 lf = __half22float2(l);
-      hi[f] = *reinterpret_cast<const uint32_t *>(&h);
-      lo[f] = *reinterpret_cast<const uint32_t *>(&l);
-      const float wgt = (f & 1) ? 1024.0f + 128.0f : 1024.0f + 8.0f;  // 1024 + 8 s
-      csum += wgt * ((hf.x + lf.x) + (hf.y + lf.y));
+      ss = warp_sum(ss);
+      if (lane == 0) s_sum[warp][m] = ss;
     }
-    uint4 *dst = xf + (bb * 2 * MV + 2 * m) * 4 + t;
-    dst[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    dst[4] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    csum += __shfl_xor_sync(0xffffffffu, csum, 1);
-    csum += __shfl_xor_sync(0xffffffffu, csum, 2);
-    if (t == 0) corr[m * nbx + bb] = -csum;
   }
   named_sync(kCThreads);
+  if (tid < MV) {
+    float s = 0.0f;
+    for (int i = 0; i < kConsumers; ++i) s += s_sum[i][tid];
+    s_inv[tid] = do_norm ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)w.K), eps))) : 1.0f;
+  }
 
   // ---------------- consume
   const int gq = lane >> 2, t = lane & 3;
-  const bool xlane = gq < 2 * MV;  // lanes holding a real B column
   const int a_off = (16 * warp + gq) * kQ4TB + t * 16;     // byte offset of row gq's lane word in a stage
+  const int par = gq & 1;                                   // quad halves swapped on odd rows
   const int d_off = GeoQ4::SQ + (16 * warp + gq) * kQ4CB * 2;
-  const uint4 *xl = xf + gq * 4 + t;                       // + block * 2MV*4
-  const float *cl = corr + t * nbx;
-  float2 acc = make_float2(0.0f, 0.0f);                    // rows gq, gq+8; token t
+  // B column gq of MMA i = digit (gq & 3) of token 2i + (gq >> 2); digit 3 is the zero column
+  const uint2 *xl[NM];
+  bool xv[NM];
+  const int *c0l[NM], *c1l[NM];
+  const float *fbl[NM];
+#pragma unroll
+  for (int im = 0; im < NM; ++im) {
+    const int btok = 2 * im + (gq >> 2), dtok = 2 * im + (t >> 1);
+    xv[im] = (gq & 3) < 3 && btok < MV;
+    xl[im] = xb + (xv[im] ? 3 * btok + (gq & 3) : 0) * 4 + t;
+    // lanes of a padding token (odd MV) read token 0's values; their D columns are dropped
+    c0l[im] = cx0 + (dtok < MV ? 4 * im + t : (t & 1)) * nbx;
+    c1l[im] = cx1 + (dtok < MV ? 4 * im + t : (t & 1)) * nbx;
+    fbl[im] = fbk + (dtok < MV ? dtok : 0) * nbx;
+  }
+  float2 acc[NM];
+#pragma unroll
+  for (int im = 0; im < NM; ++im) acc[im] = make_float2(0.0f, 0.0f);  // rows gq, gq+8
   bool ok = true;
   int i = 0, g = sc.u0 / sc.nc, c = sc.u0 % sc.nc;
   for (int u = sc.u0; u < sc.u1; ++u, ++i) {
-    const int s = i % kStages;
-    ok = ok && mbar_wait(&full[s], (uint32_t)(i / kStages) & 1, scr.err, DEVERR_GEMV_FULL);
+    const int s = i % kQ4Stages;
+    ok = ok && mbar_wait(&full[s], (uint32_t)(i / kQ4Stages) & 1, scr.err, DEVERR_GEMV_FULL);
     if (ok) {
       const unsigned char *st = ring + s * GeoQ4::SB;
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int bb0 = c * kQ4CB + 4 * j;  // first block of the quad
-        const uint4 A0 = *reinterpret_cast<const uint4 *>(st + a_off + j * 64);
-        const uint4 A1 = *reinterpret_cast<const uint4 *>(st + a_off + j * 64 + 8 * kQ4TB);
+        const uint4 A0 = *reinterpret_cast<const uint4 *>(st + a_off + (j ^ par) * 64);
+        const uint4 A1 = *reinterpret_cast<const uint4 *>(st + a_off + (j ^ par) * 64 + 8 * kQ4TB);
         const uint2 D0 = *reinterpret_cast<const uint2 *>(st + d_off + j * 8);
         const uint2 D1 = *reinterpret_cast<const uint2 *>(st + d_off + j * 8 + 8 * kQ4CB * 2);
-        float4 cr = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < MV) cr = *reinterpret_cast<const float4 *>(cl + bb0);
         const uint32_t a0w[4] = {A0.x, A0.y, A0.z, A0.w}, a1w[4] = {A1.x, A1.y, A1.z, A1.w};
-        const float crv[4] = {cr.x, cr.y, cr.z, cr.w};
 #pragma unroll
-        for (int bi = 0; bi < 4; ++bi) {
-          uint4 B = make_uint4(0u, 0u, 0u, 0u);
-          if (xlane) B = xl[(bb0 + bi) * 2 * MV * 4];
-          const uint32_t M = 0x64006400u;
-          const uint32_t wa = a0w[bi], wb = a1w[bi];
-          const uint32_t wa8 = wa >> 8, wb8 = wb >> 8;
-          const uint32_t ah0[4] = {(wa & 0x000F000Fu) | M, (wb & 0x000F000Fu) | M, (wa & 0x00F000F0u) | M,
-                                   (wb & 0x00F000F0u) | M};
-          const uint32_t ah1[4] = {(wa8 & 0x000F000Fu) | M, (wb8 & 0x000F000Fu) | M, (wa8 & 0x00F000F0u) | M,
-                                   (wb8 & 0x00F000F0u) | M};
-          float dacc[4];
-          mma_f16_zc(dacc, ah0, B.x, B.y);
-          mma_f16(dacc, ah1, B.z, B.w);
-          // scale pair (row gq, row gq+8) of block bi: halves bi of D0 and D1
-          const uint32_t dpair = __byte_perm(bi < 2 ? D0.x : D0.y, bi < 2 ? D1.x : D1.y, (bi & 1) ? 0x7632 : 0x5410);
-          const float2 dsc = __half22float2(*reinterpret_cast<const __half2 *>(&dpair));
-          float2 v = fadd2(make_float2(dacc[0], dacc[2]), make_float2(dacc[1], dacc[3]));
-          v = fadd2(v, make_float2(crv[bi], crv[bi]));
-          acc = ffma2(dsc, v, acc);
+        for (int im = 0; im < NM; ++im) {
+          const int4 C0 = *reinterpret_cast<const int4 *>(c0l[im] + bb0);
+          const int4 C1 = *reinterpret_cast<const int4 *>(c1l[im] + bb0);
+          const float4 FB = *reinterpret_cast<const float4 *>(fbl[im] + bb0);
+          const int c0v[4] = {C0.x, C0.y, C0.z, C0.w}, c1v[4] = {C1.x, C1.y, C1.z, C1.w};
+          const float fbv[4] = {FB.x, FB.y, FB.z, FB.w};
+#pragma unroll
+          for (int bi = 0; bi < 4; ++bi) {
+            uint2 B = make_uint2(0u, 0u);
+            if (xv[im]) B = xl[im][(bb0 + bi) * 3 * MV * 4];
+            const uint32_t wa = a0w[bi], wb = a1w[bi];
+            int di[4];
+            imma_u8s8(di, wa & 0x0F0F0F0Fu, wb & 0x0F0F0F0Fu, (wa >> 4) & 0x0F0F0F0Fu, (wb >> 4) & 0x0F0F0F0Fu, B.x,
+                      B.y, c0v[bi], c1v[bi]);
+            const float2 v = make_float2((float)(di[0] * 128 + di[1]), (float)(di[2] * 128 + di[3]));
+            // scale pair (row gq, row gq+8) of block bi: halves bi of D0 and D1
+            const uint32_t dpair =
+                __byte_perm(bi < 2 ? D0.x : D0.y, bi < 2 ? D1.x : D1.y, (bi & 1) ? 0x7632 : 0x5410);
+            float2 dsc = __half22float2(*reinterpret_cast<const __half2 *>(&dpair));
+            dsc = fmul2(dsc, make_float2(fbv[bi], fbv[bi]));
+            acc[im] = ffma2(dsc, v, acc[im]);
+          }
         }
       }
     }
@@ -366,14 +397,21 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     const bool group_end = (c == sc.nc - 1) || (u == sc.u1 - 1);
     if (group_end) {
-      if (t < MV) {
-        red[(16 * warp + gq) * MV + t] = acc.x * s_inv_sigma[t];
-        red[(16 * warp + gq + 8) * MV + t] = acc.y * s_inv_sigma[t];
+#pragma unroll
+      for (int im = 0; im < NM; ++im) {
+        // lanes t even hold 128 D_hi + D_mid sums, lane t + 1 the 128 D_lo sums
+        const float bx = __shfl_down_sync(0xffffffffu, acc[im].x, 1);
+        const float by = __shfl_down_sync(0xffffffffu, acc[im].y, 1);
+        const int tk = 2 * im + (t >> 1);
+        if ((t & 1) == 0 && tk < MV) {
+          red[(16 * warp + gq) * MV + tk] = acc[im].x * 128.0f + bx * 0.0078125f;
+          red[(16 * warp + gq + 8) * MV + tk] = acc[im].y * 128.0f + by * 0.0078125f;
+        }
+        acc[im] = make_float2(0.0f, 0.0f);
       }
       named_sync(kCThreads);
-      finish_group<kQ4Rows, MV>(w, ep, scr, sc, g, red, &s_last, ok);
+      finish_group<kQ4Rows, MV>(w, ep, scr, sc, g, red, s_inv, &s_last, ok);
       named_sync(kCThreads);
-      acc = make_float2(0.0f, 0.0f);
     }
     if (++c == sc.nc) {
       c = 0;
@@ -541,7 +579,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           acc[r][m] = make_float2(0.0f, 0.0f);
         }
       named_sync(kCThreads);
-      finish_group<kRows, MV>(w, ep, scr, sc, g, red, &s_last, ok);
+      finish_group<kRows, MV>(w, ep, scr, sc, g, red, nullptr, &s_last, ok);
       named_sync(kCThreads);
     }
     if (++c == sc.nc) {
@@ -556,12 +594,18 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------------------
 size_t q4_smem(int64_t K, int MV) {
   const int64_t nbx = ceil_div(K / 32, kQ4CB) * kQ4CB;
-  return 128 + (size_t)kStages * GeoQ4::SB + (size_t)nbx * 2 * MV * 4 * 16 + (size_t)MV * nbx * 4 +
-         (size_t)kQ4Rows * MV * 4;
+  const int nm = (MV + 1) / 2;
+  (void)nm;
+  return 128 + (size_t)kQ4Stages * GeoQ4::SB + (size_t)nbx * 3 * MV * 4 * 8 + (size_t)4 * MV * nbx * 4 +
+         (size_t)MV * nbx * 4 + (size_t)kQ4Rows * MV * 4;
 }
 size_t q8_smem(int64_t K, int MV) {
   return 128 + (size_t)kStages * Geo<kRows, kTileBytes, 16>::SB + (size_t)MV * K * 4 + (size_t)kRows * MV * 4;
 }
+
+// Shared memory per CTA: up to kSmemTwo two CTAs share an SM; larger x
+// staging (long K, several tokens) runs one CTA per SM with up to kSmemOne.
+constexpr size_t kSmemTwo = 112 * 1024, kSmemOne = 225 * 1024;
 
 template <int MV>
 void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, float eps, bool do_norm,
@@ -570,7 +614,8 @@ void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, f
   const int CB = q4 ? kQ4CB : 16, ROWS = q4 ? kQ4Rows : kRows, TB = q4 ? kQ4TB : kTileBytes;
   const int64_t nb = w.K / 32, nc = ceil_div(nb, CB), G = ceil_div(w.N, ROWS), U = G * nc;
   FG_REQUIRE(U < (1ll << 31), FG_ERR_SHAPE, "gemv: matrix too large");
-  const int P = (int)std::min<int64_t>(2LL * num_sms, U);
+  const size_t smem = q4 ? q4_smem(w.K, MV) : q8_smem(w.K, MV);
+  const int P = (int)std::min<int64_t>((smem <= kSmemTwo ? 2LL : 1LL) * num_sms, U);
   int maxc = 1;
   for (int64_t g = 0; g < G; ++g)
     maxc = std::max(maxc, cta_of((int)(g * nc + nc - 1), (int)U, P) - cta_of((int)(g * nc), (int)U, P) + 1);
@@ -578,18 +623,16 @@ void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, f
              "gemv: workspace too small for N=%lld K=%lld", (long long)w.N, (long long)w.K);
   GemvScratch scx = sc;
   scx.maxc = maxc;
-  const size_t smem = q4 ? q4_smem(w.K, MV) : q8_smem(w.K, MV);
-  auto kern = q4 ? k_qgemv_q4<MV> : k_qgemv_q8<MV>;
   static unsigned long long attr_set[2] = {0, 0};  // per instantiation, one bit per device
   int dev = 0;
   FG_CUDA(cudaGetDevice(&dev));
   if (!(attr_set[q4] & (1ull << dev))) {
-    FG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024));
+    if (q4)
+      FG_CUDA(cudaFuncSetAttribute(k_qgemv_q4<MV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOne));
+    else
+      FG_CUDA(cudaFuncSetAttribute(k_qgemv_q8<MV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOne));
     attr_set[q4] |= 1ull << dev;
   }
-  const CUtensorMap tq = make_tmap_2d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w.N, w.row_words, w.row_words * 4,
-                                      ROWS, TB / 4);
-  const CUtensorMap td = make_tmap_2d(w.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.N, w.ldd, w.ldd * 2, ROWS, CB);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)P);
   cfg.blockDim = dim3(kThreads);
@@ -600,7 +643,15 @@ void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, f
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FG_CUDA(cudaLaunchKernelEx(&cfg, kern, tq, td, w, x, ldx, gamma, eps, do_norm ? 1 : 0, ep, scx));
+  if (q4) {
+    FG_REQUIRE(((uintptr_t)w.qs & 15) == 0, FG_ERR_VALIDATION, "gemv: Q4_0 tiles must be 16-byte aligned");
+    FG_CUDA(cudaLaunchKernelEx(&cfg, k_qgemv_q4<MV>, w, x, ldx, gamma, eps, do_norm ? 1 : 0, ep, scx));
+  } else {
+    const CUtensorMap tq = make_tmap_2d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w.N, w.row_words, w.row_words * 4,
+                                        ROWS, TB / 4);
+    const CUtensorMap td = make_tmap_2d(w.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.N, w.ldd, w.ldd * 2, ROWS, CB);
+    FG_CUDA(cudaLaunchKernelEx(&cfg, k_qgemv_q8<MV>, tq, td, w, x, ldx, gamma, eps, do_norm ? 1 : 0, ep, scx));
+  }
 }
 
 }  // namespace
@@ -608,7 +659,7 @@ void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, f
 bool gemv_supported(const QMat &w, int M) {
   if (M < 1 || M > 4 || w.K % 32 != 0 || w.K < 32) return false;
   const size_t smem = w.qtype == FG_Q4_0 ? q4_smem(w.K, M) : q8_smem(w.K, M);
-  return smem <= 112 * 1024;
+  return smem <= kSmemOne;
 }
 
 void launch_qgemv_ld(const QMat &w, const float *x, int M, int64_t ldx, const float *norm_gamma, float norm_eps,

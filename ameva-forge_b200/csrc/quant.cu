@@ -62,20 +62,23 @@ void launch_unpack_quant(const uint32_t *packed, const float *scales, const floa
 // ---------------------------------------------------------------------------
 // GGUF blocks <-> device layout.  GGUF Q4_0 block: fp16 d, then 16 bytes where
 // byte j holds value j (low nibble) and value j+16 (high nibble).  Q8_0: fp16
-// d then 32 int8.  The device keeps the reference packing (element i in nibble
-// i%8 / byte i%4 of word i/8 / i/4, codes offset to unsigned) and fp16 scales.
-// One thread per block; the 18/34-byte source blocks are read bytewise.
+// d then 32 int8.  Q8_0 on the device keeps the reference packing (element i
+// in byte i%4 of word i/4, codes offset to unsigned) with a scale plane;
+// Q4_0 goes into the tiled layout (common.cuh), whose lane-words are the GGUF
+// qs words themselves.  One thread per block; the 18/34-byte source blocks
+// are read bytewise.
 // ---------------------------------------------------------------------------
-__global__ void k_gguf_to_device(const uint8_t *__restrict__ src, int qtype, int64_t nblocks, int64_t nbr,
-                                 int64_t ldd, int64_t row_words, int64_t dst_rs, int64_t dst_ro,
-                                 uint32_t *__restrict__ qs, __half *__restrict__ d) {
+__global__ void k_gguf_to_device(const uint8_t *__restrict__ src, QMat w, int64_t nblocks, int64_t nbr,
+                                 int64_t dst_rs, int64_t dst_ro) {
+  uint32_t *qs = const_cast<uint32_t *>(w.qs);
+  __half *d = const_cast<__half *>(w.d);
   for (int64_t sb = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; sb < nblocks; sb += (int64_t)gridDim.x * blockDim.x) {
     // source block sb = (row r, column block cb); destination row r * dst_rs + dst_ro
     const int64_t drow = (sb / nbr) * dst_rs + dst_ro, cb = sb % nbr;
-    const int64_t b = drow * nbr + cb;      // qs block index
-    const int64_t db = drow * ldd + cb;     // scale index (padded rows)
+    const int64_t b = drow * nbr + cb;      // Q8_0 qs block index
+    const int64_t db = qmat_scale_at(w, drow, cb);
     const int64_t src_b = sb;
-    if (qtype == FG_Q4_0) {
+    if (w.qtype == FG_Q4_0) {
       const uint8_t *blk = src + 18 * src_b;
       uint8_t code[32];
 #pragma unroll
@@ -85,9 +88,8 @@ __global__ void k_gguf_to_device(const uint8_t *__restrict__ src, int qtype, int
       }
       uint32_t ws[4];
       q4_pack(code, ws);
-      uint32_t *row = qs + drow * row_words;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) row[q4_word(cb, t)] = ws[t];
+      for (int t = 0; t < 4; ++t) qs[q4_word_at(w, drow, cb, t)] = ws[t];
       d[db] = __ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8)));
     } else {
       const uint8_t *blk = src + 34 * src_b;
@@ -114,24 +116,21 @@ void launch_gguf_to_device(const uint8_t *blocks, int qtype, int64_t N, int64_t 
   FG_REQUIRE(dst.K == K && dst.qtype == qtype && (N - 1) * dst_rs + dst_ro < dst.N, FG_ERR_SHAPE,
              "quant repack: destination does not fit");
   int grid = (int)std::min<int64_t>(ceil_div(nb, 256), 148 * 16);
-  k_gguf_to_device<<<grid, 256, 0, s>>>(blocks, qtype, nb, K / 32, dst.ldd, dst.row_words, dst_rs, dst_ro,
-                                        const_cast<uint32_t *>(dst.qs), const_cast<__half *>(dst.d));
+  k_gguf_to_device<<<grid, 256, 0, s>>>(blocks, dst, nb, K / 32, dst_rs, dst_ro);
   FG_LAUNCH_CHECK();
 }
 
-__global__ void k_device_to_gguf(const uint32_t *__restrict__ qs, const __half *__restrict__ d, int qtype,
-                                 int64_t nblocks, int64_t nbr, int64_t ldd, int64_t row_words,
-                                 uint8_t *__restrict__ dst) {
+__global__ void k_device_to_gguf(QMat w, int64_t nblocks, int64_t nbr, uint8_t *__restrict__ dst) {
   for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks; b += (int64_t)gridDim.x * blockDim.x) {
-    unsigned short dh = __half_as_ushort(d[(b / nbr) * ldd + b % nbr]);
-    if (qtype == FG_Q4_0) {
+    const int64_t r = b / nbr, cb = b % nbr;
+    unsigned short dh = __half_as_ushort(w.d[qmat_scale_at(w, r, cb)]);
+    if (w.qtype == FG_Q4_0) {
       uint8_t *blk = dst + 18 * b;
       blk[0] = dh & 0xFF;
       blk[1] = dh >> 8;
       uint32_t ws[4];
-      const uint32_t *row = qs + (b / nbr) * row_words;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) ws[t] = row[q4_word(b % nbr, t)];
+      for (int t = 0; t < 4; ++t) ws[t] = w.qs[q4_word_at(w, r, cb, t)];
       uint8_t code[32];
       q4_unpack(ws, code);
 #pragma unroll
@@ -140,9 +139,9 @@ __global__ void k_device_to_gguf(const uint32_t *__restrict__ qs, const __half *
       uint8_t *blk = dst + 34 * b;
       blk[0] = dh & 0xFF;
       blk[1] = dh >> 8;
-      const uint32_t *w = qs + 8 * b;
+      const uint32_t *q = w.qs + 8 * b;
 #pragma unroll
-      for (int j = 0; j < 32; ++j) blk[2 + j] = (uint8_t)(((w[j / 4] >> (8 * (j % 4))) & 0xFFu) ^ 0x80u);
+      for (int j = 0; j < 32; ++j) blk[2 + j] = (uint8_t)(((q[j / 4] >> (8 * (j % 4))) & 0xFFu) ^ 0x80u);
     }
   }
 }
@@ -151,7 +150,7 @@ void launch_device_to_gguf(const QMat &w, uint8_t *blocks, cudaStream_t s) {
   int64_t nb = w.N * (w.K / 32);
   if (nb == 0) return;
   int grid = (int)std::min<int64_t>(ceil_div(nb, 256), 148 * 16);
-  k_device_to_gguf<<<grid, 256, 0, s>>>(w.qs, w.d, w.qtype, nb, w.K / 32, w.ldd, w.row_words, blocks);
+  k_device_to_gguf<<<grid, 256, 0, s>>>(w, nb, w.K / 32, blocks);
   FG_LAUNCH_CHECK();
 }
 
@@ -160,17 +159,15 @@ void launch_device_to_gguf(const QMat &w, uint8_t *blocks, cudaStream_t s) {
 // roundings as the reference unpack on the mapped operands (zero 8 / 128).
 // One thread per 32-value block; 8 x 16-byte stores.
 // ---------------------------------------------------------------------------
-__global__ void k_dequant(const uint32_t *__restrict__ qs, const __half *__restrict__ d, int qtype, int64_t nblocks,
-                          int64_t nbr, int64_t ldd, int64_t row_words, float *__restrict__ out) {
+__global__ void k_dequant(QMat w, int64_t nblocks, int64_t nbr, float *__restrict__ out) {
   for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < nblocks; b += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = b / nbr, cb = b % nbr;
-    const float sc = __half2float(d[r * ldd + cb]);
-    const uint32_t *row = qs + r * row_words;
+    const float sc = __half2float(w.d[qmat_scale_at(w, r, cb)]);
     float v[32];
-    if (qtype == FG_Q4_0) {
+    if (w.qtype == FG_Q4_0) {
       uint32_t ws[4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) ws[t] = row[q4_word(cb, t)];
+      for (int t = 0; t < 4; ++t) ws[t] = w.qs[q4_word_at(w, r, cb, t)];
       uint8_t code[32];
       q4_unpack(ws, code);
 #pragma unroll
@@ -178,9 +175,9 @@ __global__ void k_dequant(const uint32_t *__restrict__ qs, const __half *__restr
     } else {
 #pragma unroll
       for (int t = 0; t < 8; ++t) {
-        const uint32_t w = row[cb * 8 + t];
+        const uint32_t q = w.qs[r * w.row_words + cb * 8 + t];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) v[4 * t + k] = __fmul_rn(__fsub_rn((float)((w >> (8 * k)) & 0xFFu), 128.0f), sc);
+        for (int k = 0; k < 4; ++k) v[4 * t + k] = __fmul_rn(__fsub_rn((float)((q >> (8 * k)) & 0xFFu), 128.0f), sc);
       }
     }
     float4 *o = reinterpret_cast<float4 *>(out + 32 * b);
@@ -193,7 +190,7 @@ void launch_dequant(const QMat &w, float *out, cudaStream_t s) {
   const int64_t nb = w.N * (w.K / 32);
   if (nb == 0) return;
   int grid = (int)std::min<int64_t>(ceil_div(nb, 128), 148 * 16);
-  k_dequant<<<grid, 128, 0, s>>>(w.qs, w.d, w.qtype, nb, w.K / 32, w.ldd, w.row_words, out);
+  k_dequant<<<grid, 128, 0, s>>>(w, nb, w.K / 32, out);
   FG_LAUNCH_CHECK();
 }
 
@@ -223,14 +220,15 @@ void launch_synth_normal(uint64_t seed, uint64_t offset, int64_t n, float mean, 
 // N01(seed, (row0 + r) * K + c)).  Q4_0: d = v_absmax / -8, code =
 // min(15, trunc(v / d + 8.5)); Q8_0: d = absmax / 127, q = round(v / d).
 __global__ void k_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, int64_t row0, int64_t col0,
-                              int64_t k_full, float stdv, int64_t dst_rs, int64_t dst_ro, int64_t ldd,
-                              int64_t row_words, uint32_t *__restrict__ qs, __half *__restrict__ dsc) {
+                              int64_t k_full, float stdv, int64_t dst_rs, int64_t dst_ro, QMat dst) {
+  uint32_t *qs = const_cast<uint32_t *>(dst.qs);
+  __half *dsc = const_cast<__half *>(dst.d);
   const int64_t nbr = K / 32;
   const int64_t nb = N * nbr;
   for (int64_t sb = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; sb < nb; sb += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = sb / nbr, cb = sb % nbr;
-    const int64_t b = (r * dst_rs + dst_ro) * nbr + cb;
-    const int64_t db = (r * dst_rs + dst_ro) * ldd + cb;
+    const int64_t drow = r * dst_rs + dst_ro;
+    const int64_t db = qmat_scale_at(dst, drow, cb);
     const uint64_t base = (uint64_t)(row0 + r) * (uint64_t)k_full + (uint64_t)col0 + (uint64_t)cb * 32;
     float v[32];
     float amax = 0.0f, vmax = 0.0f;
@@ -254,9 +252,8 @@ __global__ void k_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, in
       }
       uint32_t w[4];
       q4_pack(code, w);
-      uint32_t *row = qs + (r * dst_rs + dst_ro) * row_words;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) row[q4_word(cb, t)] = w[t];
+      for (int t = 0; t < 4; ++t) qs[q4_word_at(dst, drow, cb, t)] = w[t];
       dsc[db] = __float2half_rn(dd);
     } else {
       float dd = __fdiv_rn(amax, 127.0f);
@@ -267,7 +264,7 @@ __global__ void k_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, in
         int q = (int)roundf(__fmul_rn(v[j], id));
         w[j / 4] |= (uint32_t)(uint8_t)(q + 128) << (8 * (j % 4));
       }
-      uint4 *o = reinterpret_cast<uint4 *>(qs + (r * dst_rs + dst_ro) * row_words) + 2 * cb;
+      uint4 *o = reinterpret_cast<uint4 *>(qs + drow * dst.row_words) + 2 * cb;
       o[0] = make_uint4(w[0], w[1], w[2], w[3]);
       o[1] = make_uint4(w[4], w[5], w[6], w[7]);
       dsc[db] = __float2half_rn(dd);
@@ -282,8 +279,7 @@ void launch_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, int64_t 
   FG_REQUIRE(dst.K == K && dst.qtype == qtype && (N - 1) * dst_rs + dst_ro < dst.N, FG_ERR_SHAPE,
              "synthetic quant: destination does not fit");
   int grid = (int)std::min<int64_t>(ceil_div(nb, 128), 148 * 16);
-  k_synth_quant<<<grid, 128, 0, s>>>(qtype, N, K, seed, row0, col0, k_full, stdv, dst_rs, dst_ro, dst.ldd, dst.row_words,
-                                     const_cast<uint32_t *>(dst.qs), const_cast<__half *>(dst.d));
+  k_synth_quant<<<grid, 128, 0, s>>>(qtype, N, K, seed, row0, col0, k_full, stdv, dst_rs, dst_ro, dst);
   FG_LAUNCH_CHECK();
 }
 
