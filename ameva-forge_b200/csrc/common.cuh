@@ -105,53 +105,56 @@ __device__ inline float normal01(uint64_t seed, uint64_t i) {
 //   per 32-element block, [N][ldd] after qs (256-byte aligned), rows padded to
 //   a multiple of 8 scales (16 bytes) for the TMA row pitch.
 //
-// Q4_0 -- tiles of 128 rows x 8 blocks (18,432 bytes each), so that the GEMV
-//   streams each tile with one contiguous bulk copy.  Tile (g, c) holds rows
-//   128g.. and blocks 8c..; tiles are stored row-group major ([g][c]), rows
-//   and blocks past N and K/32 are zero.  Inside a tile:
-//     bytes [0, 16384): codes (q + 8), 128 bytes per row: the 16 words of
-//       block quad j (blocks 4j..4j+3) sit at 64-byte half (j ^ (row & 1)) of
-//       the row (the swap puts neighbouring rows on different shared-memory
-//       banks); in a half, lane-word t of block 4j+i is word t*4 + i.  Word t
-//       of a block is GGUF bytes 4t..4t+3 of its qs: the low nibble of byte
-//       i holds element 4t + i and the high nibble element 16 + 4t + i
-//       (q4_elem) -- the k order of the int8 A fragments of mma.sync
-//       m16n8k32 (a0/a1: k = 4t..4t+3, a2/a3: k = 16+4t..16+4t+3), so a
-//       mask (and a shift) turns a word into two fragment registers;
-//     bytes [16384, 18432): fp16 scales, [128 rows][8 blocks].
-constexpr int kQ4TileRows = 128, kQ4TileBlocks = 8;
-constexpr int kQ4TileCodeBytes = kQ4TileRows * kQ4TileBlocks * 16;
-constexpr int kQ4TileBytes = kQ4TileCodeBytes + kQ4TileRows * kQ4TileBlocks * 2;
+// Q4_0 -- row strips of 16 rows, so that one GEMV worker owns whole output
+//   rows (no cross-CTA reduction).  A strip stores its blocks in quads of 4
+//   (blocks past K/32, up to a multiple of 4, are zero; rows past N are
+//   zero); quad Q of strip s is 1152 bytes at (s * quads_per_strip + Q) * 1152:
+//     bytes [0, 1024): codes (q + 8), u32 word (r * 4 + t) * 4 + i = lane-word
+//       t of block 4Q + i of row 16s + r.  Lane-word t of a block is GGUF
+//       bytes 4t..4t+3 of its qs: the low nibble of byte i holds element
+//       4t + i and the high nibble element 16 + 4t + i (q4_elem) -- the k
+//       order of the int8 A fragments of mma.sync m16n8k32 (a0/a1: k =
+//       4t..4t+3, a2/a3: k = 16+4t..16+4t+3), so a mask (and a shift) turns
+//       a word into two fragment registers, and the lane (row g, word t) of
+//       an MMA reads one 16-byte word group of 4 blocks;
+//     bytes [1024, 1152): fp16 scales, [16 rows][4 blocks].
+//   The GEMV streams a strip as tiles of up to 16 quads (18,432 bytes), each
+//   one contiguous bulk copy.
+constexpr int kQ4StripRows = 16, kQ4QuadBytes = 1152, kQ4TileQuads = 16;
+constexpr int kQ4QuadCodeBytes = 1024;
+constexpr int kQ4TileBytes = kQ4TileQuads * kQ4QuadBytes;
 struct QMat {
   const uint32_t *qs;
-  const __half *d;    // Q4_0: the allocation base (scales sit inside the tiles)
+  const __half *d;    // Q4_0: the allocation base (scales sit inside the quads)
   int32_t qtype;      // FG_Q4_0 / FG_Q8_0
   int64_t N, K;
   int64_t ldd;        // Q8_0: scales per d row (K/32 rounded up to 8)
-  int64_t row_words;  // Q8_0: u32 words per qs row; Q4_0: tiles per row group
+  int64_t row_words;  // Q8_0: u32 words per qs row; Q4_0: quads per strip
 };
 __host__ __device__ inline int64_t qmat_ldd(int64_t K) { return (K / 32 + 7) / 8 * 8; }
-__host__ __device__ inline int64_t q4_chunks(int64_t K) { return (K / 32 + kQ4TileBlocks - 1) / kQ4TileBlocks; }
-__host__ __device__ inline int64_t q4_groups(int64_t N) { return (N + kQ4TileRows - 1) / kQ4TileRows; }
+__host__ __device__ inline int64_t q4_quads(int64_t K) { return (K / 32 + 3) / 4; }
+__host__ __device__ inline int64_t q4_strips(int64_t N) { return (N + kQ4StripRows - 1) / kQ4StripRows; }
+__host__ __device__ inline int64_t q4_tiles(int64_t K) { return (q4_quads(K) + kQ4TileQuads - 1) / kQ4TileQuads; }
 __host__ __device__ inline int64_t qmat_row_words(int qtype, int64_t K) {
-  return qtype == FG_Q4_0 ? q4_chunks(K) : K / 4;
+  return qtype == FG_Q4_0 ? q4_quads(K) : K / 4;
 }
 // Block element held by nibble p of lane-word t (Q4_0 device packing).
 __host__ __device__ inline int q4_elem(int t, int p) { return 4 * t + (p >> 1) + 16 * (p & 1); }
+// Q4_0: byte offset of quad Q of the strip holding row n.
+__host__ __device__ inline int64_t q4_quad_off(const QMat &w, int64_t n, int64_t Q) {
+  return ((n / kQ4StripRows) * w.row_words + Q) * kQ4QuadBytes;
+}
 // Q4_0: u32 index (from qs) of lane-word t of block b of row n.
 __host__ __device__ inline int64_t q4_word_at(const QMat &w, int64_t n, int64_t b, int t) {
-  const int64_t tile = (n / kQ4TileRows) * w.row_words + b / kQ4TileBlocks;
-  const int r = (int)(n % kQ4TileRows), bb = (int)(b % kQ4TileBlocks);
-  return tile * (kQ4TileBytes / 4) + r * 32 + (((bb >> 2) ^ (r & 1)) << 4) + t * 4 + (bb & 3);
+  return (q4_quad_off(w, n, b >> 2) + ((n % kQ4StripRows) * 4 + t) * 16 + (b & 3) * 4) / 4;
 }
 // fp16 scale index (from d) of block b of row n, both layouts.
 __host__ __device__ inline int64_t qmat_scale_at(const QMat &w, int64_t n, int64_t b) {
   if (w.qtype != FG_Q4_0) return n * w.ldd + b;
-  const int64_t tile = (n / kQ4TileRows) * w.row_words + b / kQ4TileBlocks;
-  return tile * (kQ4TileBytes / 2) + kQ4TileCodeBytes / 2 + (n % kQ4TileRows) * kQ4TileBlocks + b % kQ4TileBlocks;
+  return (q4_quad_off(w, n, b >> 2) + kQ4QuadCodeBytes + ((n % kQ4StripRows) * 4 + (b & 3)) * 2) / 2;
 }
 inline uint64_t qmat_qs_bytes(int qtype, int64_t N, int64_t K) {
-  if (qtype == FG_Q4_0) return (uint64_t)q4_groups(N) * (uint64_t)q4_chunks(K) * kQ4TileBytes;
+  if (qtype == FG_Q4_0) return (uint64_t)q4_strips(N) * (uint64_t)q4_quads(K) * kQ4QuadBytes;
   return (uint64_t)N * (uint64_t)qmat_row_words(qtype, K) * 4;
 }
 inline uint64_t qmat_d_offset(int qtype, int64_t N, int64_t K) { return align_up(qmat_qs_bytes(qtype, N, K), 256); }

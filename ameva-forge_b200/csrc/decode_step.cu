@@ -1,0 +1,651 @@
+// Persistent decode step: one cooperative launch runs a whole greedy decode
+// step of a Llama-shaped decoder at batch 1 (tensor parallelism 1, Q4_0
+// weights, fp16 KV cache) -- the per-layer sequence of llama.py:149-165 plus
+// the embedding, the final norm + lm_head and the greedy pick:
+//
+//   EMBED | L x (QKV, ATTN, O, GATEUP, DOWN) | LM_HEAD | ARGMAX
+//
+// with a grid-wide barrier between phases.  The point of one launch is that
+// the weights and the KV cache -- which do not depend on this step's
+// activations -- stream continuously: every CTA holds two "virtual CTAs"
+// (a producer thread + 8 consumer warps + a 4-stage shared-memory ring), and
+// each producer walks the whole phase list ahead of its consumers, so while
+// the consumers wait at a barrier or stage the next activation vector, the
+// rings keep filling with the next phase's tiles.
+//
+// Phases:
+//  * GEMV phases use the Q4_0 integer-MMA GEMV of q4_gemv.cuh with the fused
+//    epilogues of the layered path (RMSNorm fused into x staging, RoPE + KV
+//    append, SwiGLU, residual add), split over the 2 x gridDim virtual CTAs
+//    exactly as the stand-alone GEMV splits them (same sums, same order);
+//  * ATTN: split-KV attention over the cache.  Unit (KV head, split) covers a
+//    run of 32-key tiles of keys [0, pos) (streamed through the ring: K tile
+//    and V tile, one bulk copy each); the unit of the last split adds key
+//    pos -- this step's K/V, written by the QKV phase -- from global memory,
+//    so the producer never waits on this step's results.  A unit's partial
+//    (max, sum, output) is merged by the last unit of its head to arrive;
+//  * ARGMAX: every CTA reduces a slice of the logits to a 64-bit key (value,
+//    then lowest index; the sampler's NaN rules, sampling.ts:45-55) and
+//    atomicMax-es it; after one more barrier CTA 0 writes the token, logs it
+//    and advances the position.
+//
+// Every wait is bounded (2 s): a barrier that times out sets the device error
+// word, and all threads then leave without further waiting.
+#include "q4_gemv.cuh"
+
+namespace fg {
+
+namespace {
+
+constexpr int kStepStages = 4;                                   // ring stages per virtual CTA
+constexpr int kStepGroups = 2;                                   // virtual CTAs per CTA
+constexpr int kStepConsumers = kStepGroups * kGroupThreads;      // 512
+constexpr int kStepThreads = kStepConsumers + kStepGroups * 32;  // + one producer warp per group
+constexpr int kKeysPerTile = 32;
+constexpr int kBarConsumers = 3;                                 // named barrier of all consumer warps
+
+enum Phase { PH_EMBED, PH_QKV, PH_ATTN, PH_O, PH_GATEUP, PH_DOWN, PH_LM, PH_ARGMAX };
+
+__device__ __forceinline__ Phase phase_kind(int p, int L) {
+  if (p == 0) return PH_EMBED;
+  if (p <= 5 * L) return (Phase)(PH_QKV + (p - 1) % 5);
+  return p == 5 * L + 1 ? PH_LM : PH_ARGMAX;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ int ld_volatile_int(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
+
+// Grid-wide barrier, one calling thread per CTA (after a CTA-wide barrier).
+// bar[0] counts arrivals and is never reset; bar[1] counts launches (the
+// epoch).  Barrier k of the launch with epoch E completes when the count
+// reaches (E * barriers_per_launch + k + 1) * CTAs, so an arrival is one
+// posted atomic add and the wait is a bounded acquire poll.
+__device__ bool grid_sync(unsigned long long *count, unsigned long long target, int *err) {
+  __threadfence();
+  atomicAdd(count, 1ull);
+  if (ld_acquire_u64(count) >= target) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    __nanosleep(32);
+    if (ld_acquire_u64(count) >= target) return true;
+    if (ld_volatile_int(err) != 0) return false;
+    if (global_ns() - t0 > kWaitTimeoutNs) {
+      atomicCAS(err, 0, DEVERR_GRID);
+      return false;
+    }
+  }
+}
+
+// Split of the attention phase: units = KV heads x splits, at most one unit per
+// virtual CTA; split s of a head covers tiles [s*nt/S, (s+1)*nt/S) of keys
+// [0, npos); the last split also takes key npos.
+struct AttnSplit {
+  int S, nt, units;
+};
+__device__ __forceinline__ AttnSplit attn_split(int npos, int Hkv, int P) {
+  AttnSplit a;
+  a.nt = (npos + kKeysPerTile - 1) / kKeysPerTile;
+  a.S = max(1, min(P / Hkv, a.nt));
+  a.units = Hkv * a.S;
+  return a;
+}
+
+}  // namespace
+
+// GEMV operand of phase p (layer l).
+__device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, QMat &w, const float *&x,
+                                           const float *&gamma, Epilogue &ep) {
+  ep = Epilogue();
+  if (ph == PH_LM) {
+    w = A.lm_head;
+    x = A.h;
+    gamma = A.norm;
+    ep.mode = EPI_PLAIN;
+    ep.y = A.logits;
+    ep.ldy = A.vocab;
+    return;
+  }
+  const StepLayer &Ly = A.layers[l];
+  switch (ph) {
+    case PH_QKV:
+      w = Ly.qkv;
+      x = A.h;
+      gamma = Ly.attn_norm;
+      ep.mode = EPI_QKV;
+      ep.q_out = A.q;
+      ep.k_cache = Ly.k;
+      ep.v_cache = Ly.v;
+      ep.n_q = A.Hq * A.d;
+      ep.n_kv = A.Hkv * A.d;
+      ep.head_dim = A.d;
+      ep.cap = A.cap;
+      ep.tokens_per_seq = 1;
+      ep.pos = A.pos;
+      ep.inv_freq = A.inv_freq;
+      break;
+    case PH_O:
+      w = Ly.o;
+      x = A.att;
+      gamma = nullptr;
+      ep.mode = EPI_PLAIN;
+      ep.y = A.h;
+      ep.resid = A.h;
+      ep.ldy = A.H;
+      break;
+    case PH_GATEUP:
+      w = Ly.gateup;
+      x = A.h;
+      gamma = Ly.ffn_norm;
+      ep.mode = EPI_SWIGLU;
+      ep.y = A.ffn;
+      ep.ldy = A.I;
+      break;
+    default:  // PH_DOWN
+      w = Ly.down;
+      x = A.ffn;
+      gamma = nullptr;
+      ep.mode = EPI_PLAIN;
+      ep.y = A.h;
+      ep.resid = A.h;
+      ep.ldy = A.H;
+      break;
+  }
+}
+
+namespace {
+
+// ---------------------------------------------------------------------------
+// Attention consumer: one unit (KV head hk, keys of tiles [t0, t1) + the
+// current key when `last`) on the 256 threads of a group.  Tile layout in a
+// ring slot: K rows [32][D] fp16, then V rows [32][D] fp16.
+// ---------------------------------------------------------------------------
+constexpr int r4(int x) { return (x + 3) & ~3; }
+
+template <int D, int G>
+struct AttnCfg {
+  static constexpr int DC = D / 8;                             // dims per lane in q.k (8 lanes per key)
+  static constexpr int PAIRS = D / 2 * G;                      // (g, dim pair) outputs
+  static constexpr int PPT = PAIRS > kGroupThreads ? PAIRS / kGroupThreads : 1;  // pairs per thread
+  static constexpr int KQ = PAIRS >= kGroupThreads ? 1 : kGroupThreads / PAIRS;   // key partitions
+  static constexpr int KPQ = kKeysPerTile / KQ;                // keys per partition
+  static_assert(D == 64 || D == 128, "head_dim");
+  // shared scratch (floats): q [G][D], scores [G][32], p [G][32], warp max [8][G], psum [G], merge [KQ][G][D]
+  static constexpr int SM_Q = 0, SM_S = G * D, SM_P = SM_S + G * 32, SM_WM = SM_P + G * 32, SM_PS = SM_WM + 8 * G,
+                       SM_O = r4(SM_PS + G), SM_END = r4(SM_O + KQ * G * D);
+};
+
+template <int D, int G>
+struct AttnState {
+  float m[G], l[G];
+  float2 o[AttnCfg<D, G>::PPT];
+};
+
+// One tile of nk keys (K at kt, V at vt in shared memory) into the state.
+template <int D, int G>
+__device__ __forceinline__ void attn_tile(const __half *kt, const __half *vt, int nk, float *sm, AttnState<D, G> &S,
+                                          int tid, int bar) {
+  using C = AttnCfg<D, G>;
+  const int lane = tid & 31, warp = tid >> 5;
+  // ---- scores: warp w takes keys 4w..4w+3, lane (kk, c) dims [c DC, (c+1) DC)
+  {
+    const int kk = lane >> 3, c = lane & 7, j = 4 * warp + kk;
+    float kf[C::DC];
+    const __half *kr = kt + j * D + c * C::DC;
+#pragma unroll
+    for (int v = 0; v < C::DC / 8; ++v) {
+      uint4 raw = make_uint4(0u, 0u, 0u, 0u);  // rows past nk are never read
+      if (j < nk) raw = *reinterpret_cast<const uint4 *>(kr + 8 * v);
+      const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __half22float2(h2[e]);
+        kf[8 * v + 2 * e] = f.x;
+        kf[8 * v + 2 * e + 1] = f.y;
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float *qg = sm + C::SM_Q + g * D + c * C::DC;
+      float s = 0.0f;
+#pragma unroll
+      for (int e = 0; e < C::DC; e += 4) {
+        const float4 q4 = *reinterpret_cast<const float4 *>(qg + e);
+        s = fmaf(q4.x, kf[e], s);
+        s = fmaf(q4.y, kf[e + 1], s);
+        s = fmaf(q4.z, kf[e + 2], s);
+        s = fmaf(q4.w, kf[e + 3], s);
+      }
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      if (j >= nk) s = -INFINITY;
+      float wm = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 8));
+      wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 16));
+      if (c == 0) sm[C::SM_S + g * 32 + j] = s;
+      if (lane == 0) sm[C::SM_WM + warp * G + g] = wm;
+    }
+  }
+  named_sync_id(bar, kGroupThreads);
+  // ---- new running max; p = exp(s - m') for (g, key) = (tid / 32, tid % 32)
+  float mnew[G], alpha[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float tm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tm = fmaxf(tm, sm[C::SM_WM + w * G + g]);
+    mnew[g] = fmaxf(S.m[g], tm);
+    alpha[g] = mnew[g] == -INFINITY ? 1.0f : expf(S.m[g] - mnew[g]);
+  }
+  for (int idx = tid; idx < G * 32; idx += kGroupThreads) {
+    const int g = idx >> 5, j = idx & 31;
+    float mg = -INFINITY;
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg)
+      if (gg == g) mg = mnew[gg];
+    const float s = sm[C::SM_S + g * 32 + j];
+    const float p = s == -INFINITY ? 0.0f : expf(s - mg);
+    sm[C::SM_P + g * 32 + j] = p;
+    const float ps = warp_sum(p);
+    if (j == 0) sm[C::SM_PS + g] = ps;
+  }
+  named_sync_id(bar, kGroupThreads);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    S.l[g] = S.l[g] * alpha[g] + sm[C::SM_PS + g];
+    S.m[g] = mnew[g];
+  }
+  // ---- o += p V: thread -> (pair slot, key partition kq)
+  const int slot = tid % (C::PAIRS / C::PPT), kq = tid / (C::PAIRS / C::PPT);
+#pragma unroll
+  for (int r = 0; r < C::PPT; ++r) {
+    const int pr = slot * C::PPT + r;       // (g, dim pair) index
+    const int g = pr / (D / 2), dp = pr % (D / 2);
+    float a = 1.0f;
+#pragma unroll
+    for (int gg = 0; gg < G; ++gg)
+      if (gg == g) a = alpha[gg];
+    float2 o = make_float2(S.o[r].x * a, S.o[r].y * a);
+    const float *pg = sm + C::SM_P + g * 32 + kq * C::KPQ;
+    const __half2 *vr = reinterpret_cast<const __half2 *>(vt + (kq * C::KPQ) * D) + dp;
+    const int kend = min(C::KPQ, nk - kq * C::KPQ);  // rows past nk are never read
+#pragma unroll 8
+    for (int j = 0; j < kend; ++j) {
+      const float p = pg[j];
+      const float2 v = __half22float2(vr[j * (D / 2)]);
+      o.x = fmaf(p, v.x, o.x);
+      o.y = fmaf(p, v.y, o.y);
+    }
+    S.o[r] = o;
+  }
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// The kernel
+// ---------------------------------------------------------------------------
+template <int D, int G>
+__global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_constant__ StepArgs A) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  unsigned char *base = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
+  __shared__ __align__(8) uint64_t full[kStepGroups][kStepStages], empty[kStepGroups][kStepStages];
+  __shared__ float s_sum[(kStepConsumers / 32)];
+  __shared__ float s_inv;
+  __shared__ int s_last[kStepGroups];
+  __shared__ int s_abort;
+  __shared__ unsigned long long s_key[kStepConsumers / 32];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int L = A.L, nphase = 5 * L + 3;
+  const int P = kStepGroups * gridDim.x;
+  unsigned char *rings = base;                                            // [2][stages][18 KB]
+  unsigned char *xarea = base + kStepGroups * kStepStages * kQ4TileBytes;  // staged x / attention scratch
+  float *reds = reinterpret_cast<float *>(xarea + A.xarea_bytes);         // [2][128]
+  const int npos = A.pos[0];                                              // keys already in the cache
+  const unsigned long long epoch = *reinterpret_cast<volatile unsigned long long *>(A.bar + 1);
+
+  if (tid == 0) {
+    for (int g = 0; g < kStepGroups; ++g)
+      for (int s = 0; s < kStepStages; ++s) {
+        mbar_init(&full[g][s], 1);
+        mbar_init(&empty[g][s], kGroupWarps);
+      }
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  // =========================== producers ===========================
+  if (tid >= kStepConsumers) {
+    const int grp = (tid - kStepConsumers) >> 5;
+    if (lane != 0) return;
+    const int vk = blockIdx.x * kStepGroups + grp;
+    unsigned char *ring = rings + grp * kStepStages * kQ4TileBytes;
+    uint64_t *fl = full[grp], *em = empty[grp];
+    const uint64_t pol = l2_evict_first_policy();
+    int i = 0;
+    bool ok = true;
+    for (int p = 0; p < nphase && ok; ++p) {
+      const Phase ph = phase_kind(p, L);
+      const int l = (p - 1) / 5;
+      if (ph == PH_ATTN) {
+        const AttnSplit sp = attn_split(npos, A.Hkv, P);
+        if (vk >= sp.units) continue;
+        const int hk = vk / sp.S, s = vk % sp.S;
+        const int t0 = s * sp.nt / sp.S, t1 = (s + 1) * sp.nt / sp.S;
+        const __half *kc = A.layers[l].k + (int64_t)hk * A.cap * D, *vc = A.layers[l].v + (int64_t)hk * A.cap * D;
+        for (int t = t0; t < t1 && ok; ++t, ++i) {
+          const int st = i % kStepStages;
+          if (i >= kStepStages && !mbar_wait(&em[st], (uint32_t)(i / kStepStages - 1) & 1, A.err, DEVERR_GEMV_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const int nk = min(kKeysPerTile, npos - t * kKeysPerTile);
+          const uint32_t bytes = (uint32_t)nk * D * 2;
+          unsigned char *slot = ring + st * kQ4TileBytes;
+          mbar_arrive_expect_tx(&fl[st], 2 * bytes);
+          bulk_g2s(slot, kc + (int64_t)t * kKeysPerTile * D, bytes, &fl[st], pol);
+          bulk_g2s(slot + kKeysPerTile * D * 2, vc + (int64_t)t * kKeysPerTile * D, bytes, &fl[st], pol);
+        }
+      } else if (ph >= PH_QKV && ph <= PH_LM && ph != PH_ATTN) {
+        QMat w;
+        const float *x, *gm;
+        Epilogue ep;
+        gemv_phase(A, ph, l, w, x, gm, ep);
+        const Sched sc = make_sched(w.N, kQ4StripRows, 1, vk, P);
+        ok = produce_q4_strips<kStepStages>(w, sc.u0, sc.u1, ring, fl, em, i, pol, A.err);
+      }
+    }
+    drain_ring<kStepStages>(fl, i, A.err);
+    return;
+  }
+
+  // =========================== consumers ===========================
+  const int grp = warp / kGroupWarps, gw = warp % kGroupWarps, gtid = tid % kGroupThreads;
+  const int vk = blockIdx.x * kStepGroups + grp;
+  const int gbar = 1 + grp;
+  unsigned char *ring = rings + grp * kStepStages * kQ4TileBytes;
+  uint64_t *fl = full[grp], *em = empty[grp];
+  float *red = reds + grp * kGroupWarps * kQ4StripRows;
+  int i = 0;  // ring stages consumed
+
+  for (int p = 0; p < nphase; ++p) {
+    const Phase ph = phase_kind(p, L);
+    const int l = (p - 1) / 5;
+    bool ok = true;
+    if (ph == PH_EMBED) {
+      const int id = A.ids[0];
+      const bool valid = id >= 0 && id < A.vocab;
+      for (int j = blockIdx.x * kStepConsumers + tid; j < A.H; j += gridDim.x * kStepConsumers)
+        A.h[j] = valid ? __half2float(A.embed[(int64_t)id * A.H + j]) : 0.0f;
+    } else if (ph == PH_ATTN) {
+      using Cf = AttnCfg<D, G>;
+      const AttnSplit sp = attn_split(npos, A.Hkv, P);
+      float *sm = reinterpret_cast<float *>(xarea) + grp * Cf::SM_END;
+      if (vk < sp.units) {
+        const int hk = vk / sp.S, s = vk % sp.S;
+        const int t0 = s * sp.nt / sp.S, t1 = (s + 1) * sp.nt / sp.S;
+        const bool last = s == sp.S - 1;
+        for (int e = gtid; e < G * D; e += kGroupThreads)
+          sm[Cf::SM_Q + e] = __ldcg(A.q + (int64_t)hk * G * D + e) * A.scale;
+        AttnState<D, G> st;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          st.m[g] = -INFINITY;
+          st.l[g] = 0.0f;
+        }
+#pragma unroll
+        for (int r = 0; r < Cf::PPT; ++r) st.o[r] = make_float2(0.0f, 0.0f);
+        named_sync_id(gbar, kGroupThreads);
+        for (int t = t0; t < t1; ++t, ++i) {
+          const int sl = i % kStepStages;
+          ok = ok && mbar_wait(&fl[sl], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
+          // every thread runs the tile (it holds group barriers); without data it takes no keys
+          const __half *kt = reinterpret_cast<const __half *>(ring + sl * kQ4TileBytes);
+          attn_tile<D, G>(kt, kt + kKeysPerTile * D, ok ? min(kKeysPerTile, npos - t * kKeysPerTile) : 0, sm, st,
+                          gtid, gbar);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&em[sl]);
+        }
+        if (last) {
+          // key npos (this step's K/V) from global memory into a one-key tile
+          __half *kt = reinterpret_cast<__half *>(reinterpret_cast<float *>(xarea) + kStepGroups * Cf::SM_END) + grp * 2 * D;
+          const __half *kg = A.layers[l].k + ((int64_t)hk * A.cap + npos) * D;
+          const __half *vg = A.layers[l].v + ((int64_t)hk * A.cap + npos) * D;
+          named_sync_id(gbar, kGroupThreads);
+          for (int e = gtid; e < D; e += kGroupThreads) {
+            kt[e] = __ldcg(kg + e);
+            kt[D + e] = __ldcg(vg + e);
+          }
+          named_sync_id(gbar, kGroupThreads);
+          attn_tile<D, G>(kt, kt + D, ok ? 1 : 0, sm, st, gtid, gbar);
+        }
+        // ---- combine the key partitions, write the unit's partial
+        float *om = sm + Cf::SM_O;  // [KQ][G][D]
+        {
+          const int slot = gtid % (Cf::PAIRS / Cf::PPT), kq = gtid / (Cf::PAIRS / Cf::PPT);
+#pragma unroll
+          for (int r = 0; r < Cf::PPT; ++r) {
+            const int pr = slot * Cf::PPT + r;
+            const int g = pr / (D / 2), dp = pr % (D / 2);
+            om[(kq * G + g) * D + 2 * dp] = st.o[r].x;
+            om[(kq * G + g) * D + 2 * dp + 1] = st.o[r].y;
+          }
+        }
+        named_sync_id(gbar, kGroupThreads);
+        float *part = A.attn_part + ((int64_t)hk * sp.S + s) * G * (D + 2);
+        for (int e = gtid; e < G * D; e += kGroupThreads) {
+          const int g = e / D, c = e % D;
+          float o = 0.0f;
+#pragma unroll
+          for (int kq = 0; kq < Cf::KQ; ++kq) o += om[(kq * G + g) * D + c];
+          if (sp.S == 1) {
+            A.att[(int64_t)(hk * G + g) * D + c] = o / fmaxf(st.l[g], 1e-12f);
+          } else {
+            part[g * (D + 2) + 2 + c] = o;
+            if (c == 0) {
+              part[g * (D + 2)] = st.m[g];
+              part[g * (D + 2) + 1] = st.l[g];
+            }
+          }
+        }
+        if (sp.S > 1) {
+          __threadfence();
+          named_sync_id(gbar, kGroupThreads);
+          if (gtid == 0) s_last[grp] = atomicAdd(A.attn_cnt + hk, 1) == sp.S - 1;
+          named_sync_id(gbar, kGroupThreads);
+          if (s_last[grp]) {
+            __threadfence();
+            const float *hp = A.attn_part + (int64_t)hk * sp.S * G * (D + 2);
+            for (int e = gtid; e < G * D; e += kGroupThreads) {
+              const int g = e / D, c = e % D;
+              float M = -INFINITY;
+              for (int q = 0; q < sp.S; ++q) M = fmaxf(M, __ldcg(hp + (q * G + g) * (D + 2)));
+              float Ls = 0.0f, O = 0.0f;
+              for (int q = 0; q < sp.S; ++q) {
+                const float mq = __ldcg(hp + (q * G + g) * (D + 2));
+                const float e2 = mq == -INFINITY ? 0.0f : expf(mq - M);
+                Ls += __ldcg(hp + (q * G + g) * (D + 2) + 1) * e2;
+                O += __ldcg(hp + (q * G + g) * (D + 2) + 2 + c) * e2;
+              }
+              A.att[(int64_t)(hk * G + g) * D + c] = O / fmaxf(Ls, 1e-12f);
+            }
+            if (gtid == 0) A.attn_cnt[hk] = 0;  // ready for the next layer
+          }
+        }
+      }
+    } else if (ph == PH_ARGMAX) {
+      // slice of the logits -> one key per CTA -> atomicMax
+      unsigned long long best = 0;
+      const int V = A.vocab;
+      for (int j = blockIdx.x * kStepConsumers + tid; j < V; j += gridDim.x * kStepConsumers) {
+        const float v = __ldcg(A.logits + j);
+        unsigned long long key;
+        if (v != v) {
+          key = j == 0 ? ~0ull : 0ull;  // a NaN never wins, except at index 0 (the sampler keeps index 0)
+        } else {
+          uint32_t bits = __float_as_uint(v);
+          bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
+          key = ((unsigned long long)bits << 32) | (0xFFFFFFFFull - (unsigned long long)j);
+        }
+        best = key > best ? key : best;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+        best = other > best ? other : best;
+      }
+      if (lane == 0) s_key[warp] = best;
+      named_sync_id(kBarConsumers, kStepConsumers);
+      if (tid == 0) {
+        unsigned long long b = 0;
+        for (int w = 0; w < kStepConsumers / 32; ++w) b = s_key[w] > b ? s_key[w] : b;
+        atomicMax(A.argkey, b);
+      }
+    } else {
+      // ---------------- GEMV phase
+      QMat w;
+      const float *x, *gm;
+      Epilogue ep;
+      gemv_phase(A, ph, l, w, x, gm, ep);
+      const Sched sc = make_sched(w.N, kQ4StripRows, 1, vk, P);  // units = 16-row strips
+      const int nq = (int)w.row_words;
+      Q4X<1> X;
+      X.carve(xarea, (int)(w.K >> 5), nq * 4);
+      q4_stage_x<1>(X, x, w.K, gm, tid, kStepConsumers, s_sum);
+      named_sync_id(kBarConsumers, kStepConsumers);
+      if (tid == 0) s_inv = rms_inv(s_sum, kStepConsumers / 32, 1, 0, w.K, A.eps, gm != nullptr);
+      named_sync_id(kBarConsumers, kStepConsumers);
+      Q4Lane<1> Ln;
+      Ln.init(X, lane);
+      float2 acc[1] = {make_float2(0.0f, 0.0f)};
+      for (int u = sc.u0; u < sc.u1; ++u) {
+        for (int q0 = 0; q0 < nq; q0 += kQ4TileQuads, ++i) {
+          const int sl = i % kStepStages;
+          ok = ok && mbar_wait(&fl[sl], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
+          if (ok) q4_tile<1>(ring + sl * kQ4TileBytes, q0, min(kQ4TileQuads, nq - q0), gw, Ln, acc);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&em[sl]);
+        }
+        q4_group_red<1>(red, acc, gw, lane);
+        named_sync_id(gbar, kGroupThreads);
+        if (ok) finish_strip<1>(w, ep, u, red, &s_inv, gtid, kGroupThreads);
+        named_sync_id(gbar, kGroupThreads);
+      }
+    }
+    // ---------------- end of phase: grid barrier
+    if (!ok) s_abort = 1;
+    named_sync_id(kBarConsumers, kStepConsumers);
+    if (tid == 0 && !s_abort &&
+        !grid_sync(A.bar, (epoch * (unsigned long long)nphase + p + 1) * gridDim.x, A.err))
+      s_abort = 1;
+    named_sync_id(kBarConsumers, kStepConsumers);
+    if (s_abort) return;
+  }
+  // ---------------- the token: CTA 0, after the ARGMAX barrier
+  if (blockIdx.x == 0 && tid == 0) {
+    const unsigned long long key = *reinterpret_cast<volatile unsigned long long *>(A.argkey);
+    const int32_t id = (int32_t)(0xFFFFFFFFull - (key & 0xFFFFFFFFull));
+    A.ids[0] = id;
+    const int st = *A.step;
+    if (A.token_log && st < A.log_steps) A.token_log[st] = id;
+    *A.step = st + 1;
+    A.pos[0] = npos + 1;
+    *A.argkey = 0ull;
+    A.bar[1] = epoch + 1;  // every CTA has passed every barrier of this launch
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+template <int D, int G>
+size_t step_attn_floats() {
+  return (size_t)kStepGroups * AttnCfg<D, G>::SM_END + (size_t)kStepGroups * D;  // + one-key tiles (2 D halves)
+}
+template <int D, int G>
+const void *step_kernel() {
+  return (const void *)k_decode_step<D, G>;
+}
+const void *pick_kernel(int D, int G) {
+  if (D == 128) {
+    switch (G) {
+      case 1: return step_kernel<128, 1>();
+      case 2: return step_kernel<128, 2>();
+      case 4: return step_kernel<128, 4>();
+      case 8: return step_kernel<128, 8>();
+    }
+  } else if (D == 64) {
+    switch (G) {
+      case 1: return step_kernel<64, 1>();
+      case 2: return step_kernel<64, 2>();
+      case 4: return step_kernel<64, 4>();
+      case 8: return step_kernel<64, 8>();
+    }
+  }
+  return nullptr;
+}
+size_t attn_floats(int D, int G) {
+  if (D == 128) {
+    switch (G) {
+      case 1: return step_attn_floats<128, 1>();
+      case 2: return step_attn_floats<128, 2>();
+      case 4: return step_attn_floats<128, 4>();
+      default: return step_attn_floats<128, 8>();
+    }
+  }
+  switch (G) {
+    case 1: return step_attn_floats<64, 1>();
+    case 2: return step_attn_floats<64, 2>();
+    case 4: return step_attn_floats<64, 4>();
+    default: return step_attn_floats<64, 8>();
+  }
+}
+}  // namespace
+
+bool decode_step_supported(int d, int G, int qtype, int64_t H, int64_t I, int64_t qdim) {
+  if (qtype != FG_Q4_0 || !pick_kernel(d, G)) return false;
+  const size_t smem = decode_step_smem(d, G, H, I, qdim);
+  return smem <= 220 * 1024;  // 227 KB per block, less the kernel's static shared memory
+}
+
+size_t decode_step_xarea(int d, int G, int64_t H, int64_t I, int64_t qdim) {
+  int64_t kmax = std::max(H, std::max(I, qdim));
+  const int nbx = (int)q4_quads(kmax) * 4;
+  const size_t xb = align_up(Q4X<1>::bytes(nbx), 16);
+  const size_t ab = align_up(attn_floats(d, G) * 4, 16);
+  return std::max(xb, ab);
+}
+
+size_t decode_step_smem(int d, int G, int64_t H, int64_t I, int64_t qdim) {
+  return 128 + (size_t)kStepGroups * kStepStages * kQ4TileBytes + decode_step_xarea(d, G, H, I, qdim) +
+         (size_t)kStepGroups * kGroupWarps * kQ4StripRows * 4;
+}
+
+int decode_step_vctas(int num_sms) { return kStepGroups * num_sms; }
+
+void launch_decode_step(const StepArgs &A, int num_sms, cudaStream_t s) {
+  const void *kern = pick_kernel(A.d, A.Hq / A.Hkv);
+  FG_REQUIRE(kern, FG_ERR_SHAPE, "decode step: head_dim %d / GQA group %d unsupported", A.d, A.Hq / A.Hkv);
+  const size_t smem = decode_step_smem(A.d, A.Hq / A.Hkv, A.H, A.I, (int64_t)A.Hq * A.d);
+  FG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)num_sms);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident at once: the grid barriers rely on it
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void *args[] = {const_cast<StepArgs *>(&A)};
+  FG_CUDA(cudaLaunchKernelExC(&cfg, kern, args));
+}
+
+}  // namespace fg

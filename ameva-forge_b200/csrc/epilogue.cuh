@@ -22,10 +22,10 @@ __device__ inline float swiglu1(float g, float u) { return __fmul_rn(__fdiv_rn(g
 __device__ inline void epi_store_pair(const Epilogue &ep, int64_t n, int m, float v0, float v1) {
   if (ep.mode == EPI_PLAIN) {
     float *y = ep.y + (int64_t)m * ep.ldy + n;
-    if (ep.resid) {
+    if (ep.resid) {  // read through L2: other SMs of a persistent kernel may have written it
       const float *r = ep.resid + (int64_t)m * ep.ldy + n;
-      v0 = __fadd_rn(r[0], v0);
-      v1 = __fadd_rn(r[1], v1);
+      v0 = __fadd_rn(__ldcg(r), v0);
+      v1 = __fadd_rn(__ldcg(r + 1), v1);
     }
     y[0] = v0;
     y[1] = v1;
@@ -62,7 +62,7 @@ __device__ inline void epi_store_pair(const Epilogue &ep, int64_t n, int m, floa
 // Single column (PLAIN only; used when a kernel's row group is odd-sized).
 __device__ inline void epi_store_one(const Epilogue &ep, int64_t n, int m, float v) {
   float *y = ep.y + (int64_t)m * ep.ldy + n;
-  if (ep.resid) v = __fadd_rn(ep.resid[(int64_t)m * ep.ldy + n], v);
+  if (ep.resid) v = __fadd_rn(__ldcg(ep.resid + (int64_t)m * ep.ldy + n), v);
   *y = v;
 }
 

@@ -29,8 +29,7 @@
 // kernel.  Q8_0 math (k_qgemv_q8): CUDA cores.  PRMT places a byte into the
 // mantissa of 2^23 (0x4B000000 | byte); one packed FADD2 removes 2^23 + 128
 // exactly and packed FFMA2 accumulates in fp32, scaled by d once per block.
-#include "epilogue.cuh"
-#include "tma.cuh"
+#include "q4_gemv.cuh"
 #include "tmap.cuh"
 
 namespace fg {
@@ -43,57 +42,12 @@ constexpr int kThreads = kCThreads + 32;  // + producer warp
 constexpr int kTileBytes = 512;  // code bytes per row per chunk (one TMA box wide)
 constexpr int kStages = 3;
 
-__device__ __forceinline__ float2 fadd2(float2 a, float2 b) { return __fadd2_rn(a, b); }
-__device__ __forceinline__ float2 fmul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
-
-// CTA that owns work unit u when U units are split evenly over P CTAs
-// (CTA k owns [k*U/P, (k+1)*U/P)).
-__host__ __device__ __forceinline__ int cta_of(int u, int U, int P) {
-  return (int)(((int64_t)(u + 1) * P + U - 1) / U - 1);
-}
-
-// Stage geometry: ROWS rows x TB code bytes (CB blocks) per TMA tile.
+// Q8_0 stage geometry: ROWS rows x TB code bytes (CB blocks) per TMA tile.
 template <int ROWS, int TB, int CB>
 struct Geo {
   static constexpr int SQ = ROWS * TB;            // code bytes per stage
   static constexpr int SB = SQ + ROWS * CB * 2;   // + scales
 };
-
-struct Sched {
-  int nc, G, U, P, u0, u1;
-};
-template <int ROWS>
-__device__ __forceinline__ Sched schedule(const QMat &w, int nb_chunked) {
-  Sched s;
-  s.nc = nb_chunked;
-  s.G = (int)((w.N + ROWS - 1) / ROWS);
-  s.U = s.G * s.nc;
-  s.P = gridDim.x;
-  s.u0 = (int)((int64_t)blockIdx.x * s.U / s.P);
-  s.u1 = (int)(((int64_t)blockIdx.x + 1) * s.U / s.P);
-  return s;
-}
-
-// Producer thread, Q4_0: unit u is tile u of the tiled layout (common.cuh),
-// one contiguous bulk copy; a CTA's units are consecutive tiles, so each CTA
-// streams one contiguous range of the matrix.
-template <int STAGES>
-__device__ __forceinline__ void produce_tiles(const unsigned char *tiles, const Sched &sc, unsigned char *ring,
-                                              uint64_t *full, uint64_t *empty, int *err) {
-  const uint64_t pol = l2_evict_first_policy();
-  int i = 0;
-  for (int u = sc.u0; u < sc.u1; ++u, ++i) {
-    const int s = i % STAGES;
-    const uint32_t k = (uint32_t)(i / STAGES);
-    if (i >= STAGES && !mbar_wait(&empty[s], (k - 1) & 1, err, DEVERR_GEMV_EMPTY)) break;
-    mbar_arrive_expect_tx(&full[s], kQ4TileBytes);
-    bulk_g2s(ring + s * kQ4TileBytes, tiles + (int64_t)u * kQ4TileBytes, kQ4TileBytes, &full[s], pol);
-  }
-  // drain: no copy may still be landing in this CTA's shared memory on exit
-  for (int j = i > STAGES ? i - STAGES : 0; j < i; ++j)
-    mbar_wait(&full[j % STAGES], (uint32_t)(j / STAGES) & 1, err, DEVERR_DRAIN);
-}
 
 // Producer thread, Q8_0: stream the units [u0, u1) through the ring with 2-D
 // tensor-map loads of the codes and scales.
@@ -123,94 +77,10 @@ __device__ __forceinline__ void produce(const CUtensorMap *tq, const CUtensorMap
     mbar_wait(&full[j % kStages], (uint32_t)(j / kStages) & 1, err, DEVERR_DRAIN);
 }
 
-// Finish row group g from the CTA's partial vector red[ROWS][MV] (already
-// reduced over this CTA's warps): epilogue directly, or stream-K fix-up.
-template <int ROWS, int MV>
-__device__ __forceinline__ void finish_group(const QMat &w, const Epilogue &ep, const GemvScratch &scr,
-                                             const Sched &sc, int g, const float *red, const float *mul, int *s_last,
-                                             bool ok) {
-  constexpr int kRows = ROWS;
-  const int tid = threadIdx.x;
-  const int first = g * sc.nc, last = first + sc.nc - 1;
-  const bool whole = first >= sc.u0 && last < sc.u1;
-  float *pg = nullptr;
-  int ncontrib = 1;
-  if (!whole) {
-    const int k0 = cta_of(first, sc.U, sc.P), k1 = cta_of(last, sc.U, sc.P);
-    const int j = blockIdx.x - k0;
-    ncontrib = k1 - k0 + 1;
-    pg = scr.part + (int64_t)g * scr.maxc * kRows * MV;
-    for (int i = tid; i < kRows * MV; i += kCThreads) pg[j * kRows * MV + i] = red[i];
-    __threadfence();
-    named_sync(kCThreads);
-    if (tid == 0) *s_last = atomicAdd(scr.tickets + g, 1) == ncontrib - 1;
-    named_sync(kCThreads);
-    if (!*s_last) return;
-    __threadfence();
-    if (tid == 0) scr.tickets[g] = 0;  // ready for the next launch
-  }
-  if (!ok) return;
-  // thread -> (row pair p, token m): pairs finish RoPE / SwiGLU epilogues
-  for (int q = tid; q < (kRows / 2) * MV; q += kCThreads) {
-    const int p = q / MV, m = q % MV;
-    float v0 = 0.0f, v1 = 0.0f;
-    if (whole) {
-      v0 = red[(2 * p) * MV + m];
-      v1 = red[(2 * p + 1) * MV + m];
-    } else {
-      for (int jj = 0; jj < ncontrib; ++jj) {
-        v0 += __ldcg(pg + jj * kRows * MV + (2 * p) * MV + m);
-        v1 += __ldcg(pg + jj * kRows * MV + (2 * p + 1) * MV + m);
-      }
-    }
-    if (mul) {
-      v0 *= mul[m];
-      v1 *= mul[m];
-    }
-    const int64_t n = (int64_t)g * kRows + 2 * p;
-    if (n + 1 < w.N)
-      epi_store_pair(ep, n, m, v0, v1);
-    else if (n < w.N && ep.mode == EPI_PLAIN)
-      epi_store_one(ep, n, m, v0);
-  }
-}
-
 // ---------------------------------------------------------------------------
-// Q4_0 tensor-core GEMV (integer MMA).  128-row groups; warp w owns rows
-// 16w..16w+15 of the group for the whole K sweep (no cross-warp reduction); a
-// stage is one tile (128 rows x 8 blocks), one mma.sync m16n8k32 per block
-// and 16 rows: A = the u8 codes (q + 8, straight from the GGUF bytes), B = two
-// s8 digit columns per token, D = exact int32 dot products.
-//
-// x staging: every 32-element block of x' (x, times gamma when the RMSNorm is
-// fused) gets a power-of-two scale 2^e with max|x'| 2^e in [2^20, 2^21);
-// v = rn(x' 2^e) (22 bits) splits into digits hi = v >> 14 in [-128, 127],
-// mid = (v >> 7) & 127 and lo = v & 127.  A token takes four B columns (hi,
-// mid, lo, 0), so one MMA serves two tokens; the lanes of D columns (hi, mid)
-// accumulate 128 D_hi + D_mid, those of (lo, 0) accumulate 128 D_lo, and the
-// two combine exactly at the end as 128 a + b / 128.  The MMA accumulator
-// input is -8 * (sum of the block's digits), which removes the code offset
-// exactly, so D = sum (q - 8) * digit, and per block and row the kernel adds
-// d * 2^-e * D' into an fp32 accumulator.  Scales are local to a block, so
-// one large activation does not coarsen the others.  The RMSNorm's 1/rms
-// multiplies the finished sums.
+// Q4_0 tensor-core GEMV (q4_gemv.cuh): a CTA owns consecutive 16-row strips.
 // ---------------------------------------------------------------------------
-constexpr int kQ4Rows = kQ4TileRows, kQ4TB = 128, kQ4CB = kQ4TileBlocks;
 constexpr int kQ4Stages = 4;
-using GeoQ4 = Geo<kQ4Rows, kQ4TB, kQ4CB>;
-static_assert(GeoQ4::SB == kQ4TileBytes && GeoQ4::SQ == kQ4TileCodeBytes, "stage = one Q4_0 tile");
-
-__device__ __forceinline__ void imma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
-                                          uint32_t b1, int c0, int c1) {
-  asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"
-      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
-}
-
-// Digits of 4 consecutive elements packed as s8 bytes.
-__device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
-  return (uint32_t)(a & 0xFF) | ((uint32_t)(b & 0xFF) << 8) | ((uint32_t)(c & 0xFF) << 16) | ((uint32_t)d << 24);
-}
 
 template <int MV>
 __global__ void __launch_bounds__(kThreads, 2)
@@ -219,20 +89,15 @@ __global__ void __launch_bounds__(kThreads, 2)
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char *ring = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
   __shared__ __align__(8) uint64_t full[kQ4Stages], empty[kQ4Stages];
-  __shared__ float s_sum[kConsumers][MV];
+  __shared__ float s_sum[kConsumers * MV];
   __shared__ float s_inv[MV];
-  __shared__ int s_last;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int nb = (int)(w.K >> 5);
-  const Sched sc = schedule<kQ4Rows>(w, (nb + kQ4CB - 1) / kQ4CB);
-  const int nbx = sc.nc * kQ4CB;  // blocks staged (zero past nb)
-  constexpr int NM = (MV + 1) / 2;  // MMAs per block: two tokens each
-  uint2 *xb = reinterpret_cast<uint2 *>(ring + kQ4Stages * GeoQ4::SB);  // [nbx][3 MV digit cols][4 t]
-  int *cx0 = reinterpret_cast<int *>(xb + nbx * 3 * MV * 4);            // [2 MV][nbx] MMA C, col 2t
-  int *cx1 = cx0 + 2 * MV * nbx;                                        // [2 MV][nbx] MMA C, col 2t+1
-  float *fbk = reinterpret_cast<float *>(cx1 + 2 * MV * nbx);           // [MV][nbx] 2^-e
-  float *red = fbk + MV * nbx;                                          // [128][MV]
+  const int nb = (int)(w.K >> 5), nq = (int)w.row_words;
+  const Sched sc = make_sched(w.N, kQ4StripRows, 1, blockIdx.x, gridDim.x);  // units = strips
+  Q4X<MV> X;
+  X.carve(ring + kQ4Stages * kQ4TileBytes, nb, nq * 4);
+  float *red = reinterpret_cast<float *>(ring + kQ4Stages * kQ4TileBytes + Q4X<MV>::bytes(X.nbx));  // [8][16][MV]
 
   if (tid == 0) {
     for (int s = 0; s < kQ4Stages; ++s) {
@@ -247,176 +112,40 @@ __global__ void __launch_bounds__(kThreads, 2)
   // kernel finishes (they wait for this kernel's results before reading x).
   asm volatile("griddepcontrol.launch_dependents;");
   if (warp == kConsumers) {
-    if (lane == 0)
-      produce_tiles<kQ4Stages>(reinterpret_cast<const unsigned char *>(w.qs), sc, ring, full, empty, scr.err);
+    if (lane == 0) {
+      int i = 0;
+      produce_q4_strips<kQ4Stages>(w, sc.u0, sc.u1, ring, full, empty, i, l2_evict_first_policy(), scr.err);
+      drain_ring<kQ4Stages>(full, i, scr.err);
+    }
     return;
   }
 
   // ---------------- stage x (after the producer of x has finished)
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  {
-    const int q = lane & 7;  // 4-element group of the block; 8 lanes per block
-#pragma unroll
-    for (int m = 0; m < MV; ++m) {
-      float ss = 0.0f;
-      for (int item = tid; item < nbx * 8; item += kCThreads) {
-        const int bb = item >> 3;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (bb < nb) {
-          const int k = bb * 32 + 4 * q;
-          v = *reinterpret_cast<const float4 *>(x + m * ldx + k);
-          ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-          if (do_norm && gamma) {
-            const float4 g = *reinterpret_cast<const float4 *>(gamma + k);
-            v.x *= g.x;
-            v.y *= g.y;
-            v.z *= g.z;
-            v.w *= g.w;
-          }
-        }
-        float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-        // amax in [2^E, 2^(E+1)) -> scale 2^(20 - E); zero / subnormal blocks keep 2^126 (digits ~0)
-        const int E = ((__float_as_int(amax) >> 23) & 0xFF) - 127;
-        const int e = min(max(20 - E, -126), 126);
-        const float scl = __int_as_float((e + 127) << 23);
-        const float vf[4] = {v.x, v.y, v.z, v.w};
-        int hi[4], mi[4], lo[4], shi = 0, smi = 0, slo = 0;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int vi = __float2int_rn(fminf(fmaxf(vf[i] * scl, -2097152.0f), 2097151.0f));
-          hi[i] = vi >> 14;
-          mi[i] = (vi >> 7) & 127;
-          lo[i] = vi & 127;
-          shi += hi[i];
-          smi += mi[i];
-          slo += lo[i];
-        }
-        {
-          // B fragment words of digit columns 3m, 3m+1, 3m+2: lane-word t = q & 3, half q >> 2
-          uint32_t *col = reinterpret_cast<uint32_t *>(xb + (bb * 3 * MV + 3 * m) * 4) + (q & 3) * 2 + (q >> 2);
-          col[0] = pack_s8x4(hi[0], hi[1], hi[2], hi[3]);
-          col[8] = pack_s8x4(mi[0], mi[1], mi[2], mi[3]);
-          col[16] = pack_s8x4(lo[0], lo[1], lo[2], lo[3]);
-        }
-#pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
-          shi += __shfl_xor_sync(0xffffffffu, shi, o);
-          smi += __shfl_xor_sync(0xffffffffu, smi, o);
-          slo += __shfl_xor_sync(0xffffffffu, slo, o);
-        }
-        if (q == 0) {
-          // C of the lanes holding (hi, mid) and (lo, 0) of token m
-          cx0[(2 * m) * nbx + bb] = -8 * shi;
-          cx1[(2 * m) * nbx + bb] = -8 * smi;
-          cx0[(2 * m + 1) * nbx + bb] = -8 * slo;
-          cx1[(2 * m + 1) * nbx + bb] = 0;
-          // non-finite inputs make the block factor NaN, so the outputs are NaN
-          fbk[m * nbx + bb] = amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000);
-        }
-      }
-      ss = warp_sum(ss);
-      if (lane == 0) s_sum[warp][m] = ss;
-    }
-  }
+  q4_stage_x<MV>(X, x, ldx, do_norm ? gamma : nullptr, tid, kCThreads, s_sum);
   named_sync(kCThreads);
-  if (tid < MV) {
-    float s = 0.0f;
-    for (int i = 0; i < kConsumers; ++i) s += s_sum[i][tid];
-    s_inv[tid] = do_norm ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)w.K), eps))) : 1.0f;
-  }
+  if (tid < MV) s_inv[tid] = rms_inv(s_sum, kConsumers, MV, tid, w.K, eps, do_norm);
 
   // ---------------- consume
-  const int gq = lane >> 2, t = lane & 3;
-  const int a_off = (16 * warp + gq) * kQ4TB + t * 16;     // byte offset of row gq's lane word in a stage
-  const int par = gq & 1;                                   // quad halves swapped on odd rows
-  const int d_off = GeoQ4::SQ + (16 * warp + gq) * kQ4CB * 2;
-  // B column gq of MMA i = digit (gq & 3) of token 2i + (gq >> 2); digit 3 is the zero column
-  const uint2 *xl[NM];
-  bool xv[NM];
-  const int *c0l[NM], *c1l[NM];
-  const float *fbl[NM];
+  Q4Lane<MV> L;
+  L.init(X, lane);
+  float2 acc[Q4X<MV>::NM];
 #pragma unroll
-  for (int im = 0; im < NM; ++im) {
-    const int btok = 2 * im + (gq >> 2), dtok = 2 * im + (t >> 1);
-    xv[im] = (gq & 3) < 3 && btok < MV;
-    xl[im] = xb + (xv[im] ? 3 * btok + (gq & 3) : 0) * 4 + t;
-    // lanes of a padding token (odd MV) read token 0's values; their D columns are dropped
-    c0l[im] = cx0 + (dtok < MV ? 4 * im + t : (t & 1)) * nbx;
-    c1l[im] = cx1 + (dtok < MV ? 4 * im + t : (t & 1)) * nbx;
-    fbl[im] = fbk + (dtok < MV ? dtok : 0) * nbx;
-  }
-  float2 acc[NM];
-#pragma unroll
-  for (int im = 0; im < NM; ++im) acc[im] = make_float2(0.0f, 0.0f);  // rows gq, gq+8
+  for (int im = 0; im < Q4X<MV>::NM; ++im) acc[im] = make_float2(0.0f, 0.0f);
   bool ok = true;
-  int i = 0, g = sc.u0 / sc.nc, c = sc.u0 % sc.nc;
-  for (int u = sc.u0; u < sc.u1; ++u, ++i) {
-    const int s = i % kQ4Stages;
-    ok = ok && mbar_wait(&full[s], (uint32_t)(i / kQ4Stages) & 1, scr.err, DEVERR_GEMV_FULL);
-    if (ok) {
-      const unsigned char *st = ring + s * GeoQ4::SB;
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int bb0 = c * kQ4CB + 4 * j;  // first block of the quad
-        const uint4 A0 = *reinterpret_cast<const uint4 *>(st + a_off + (j ^ par) * 64);
-        const uint4 A1 = *reinterpret_cast<const uint4 *>(st + a_off + (j ^ par) * 64 + 8 * kQ4TB);
-        const uint2 D0 = *reinterpret_cast<const uint2 *>(st + d_off + j * 8);
-        const uint2 D1 = *reinterpret_cast<const uint2 *>(st + d_off + j * 8 + 8 * kQ4CB * 2);
-        const uint32_t a0w[4] = {A0.x, A0.y, A0.z, A0.w}, a1w[4] = {A1.x, A1.y, A1.z, A1.w};
-#pragma unroll
-        for (int im = 0; im < NM; ++im) {
-          const int4 C0 = *reinterpret_cast<const int4 *>(c0l[im] + bb0);
-          const int4 C1 = *reinterpret_cast<const int4 *>(c1l[im] + bb0);
-          const float4 FB = *reinterpret_cast<const float4 *>(fbl[im] + bb0);
-          const int c0v[4] = {C0.x, C0.y, C0.z, C0.w}, c1v[4] = {C1.x, C1.y, C1.z, C1.w};
-          const float fbv[4] = {FB.x, FB.y, FB.z, FB.w};
-#pragma unroll
-          for (int bi = 0; bi < 4; ++bi) {
-            uint2 B = make_uint2(0u, 0u);
-            if (xv[im]) B = xl[im][(bb0 + bi) * 3 * MV * 4];
-            const uint32_t wa = a0w[bi], wb = a1w[bi];
-            int di[4];
-            imma_u8s8(di, wa & 0x0F0F0F0Fu, wb & 0x0F0F0F0Fu, (wa >> 4) & 0x0F0F0F0Fu, (wb >> 4) & 0x0F0F0F0Fu, B.x,
-                      B.y, c0v[bi], c1v[bi]);
-            const float2 v = make_float2((float)(di[0] * 128 + di[1]), (float)(di[2] * 128 + di[3]));
-            // scale pair (row gq, row gq+8) of block bi: halves bi of D0 and D1
-            const uint32_t dpair =
-                __byte_perm(bi < 2 ? D0.x : D0.y, bi < 2 ? D1.x : D1.y, (bi & 1) ? 0x7632 : 0x5410);
-            float2 dsc = __half22float2(*reinterpret_cast<const __half2 *>(&dpair));
-            dsc = fmul2(dsc, make_float2(fbv[bi], fbv[bi]));
-            acc[im] = ffma2(dsc, v, acc[im]);
-          }
-        }
-      }
+  int i = 0;
+  for (int u = sc.u0; u < sc.u1; ++u) {
+    for (int q0 = 0; q0 < nq; q0 += kQ4TileQuads, ++i) {
+      const int s = i % kQ4Stages;
+      ok = ok && mbar_wait(&full[s], (uint32_t)(i / kQ4Stages) & 1, scr.err, DEVERR_GEMV_FULL);
+      if (ok) q4_tile<MV>(ring + s * kQ4TileBytes, q0, min(kQ4TileQuads, nq - q0), warp, L, acc);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-
-    const bool group_end = (c == sc.nc - 1) || (u == sc.u1 - 1);
-    if (group_end) {
-#pragma unroll
-      for (int im = 0; im < NM; ++im) {
-        // lanes t even hold 128 D_hi + D_mid sums, lane t + 1 the 128 D_lo sums
-        const float bx = __shfl_down_sync(0xffffffffu, acc[im].x, 1);
-        const float by = __shfl_down_sync(0xffffffffu, acc[im].y, 1);
-        const int tk = 2 * im + (t >> 1);
-        if ((t & 1) == 0 && tk < MV) {
-          red[(16 * warp + gq) * MV + tk] = acc[im].x * 128.0f + bx * 0.0078125f;
-          red[(16 * warp + gq + 8) * MV + tk] = acc[im].y * 128.0f + by * 0.0078125f;
-        }
-        acc[im] = make_float2(0.0f, 0.0f);
-      }
-      named_sync(kCThreads);
-      finish_group<kQ4Rows, MV>(w, ep, scr, sc, g, red, s_inv, &s_last, ok);
-      named_sync(kCThreads);
-    }
-    if (++c == sc.nc) {
-      c = 0;
-      ++g;
-    }
+    q4_group_red<MV>(red, acc, warp, lane);
+    named_sync(kCThreads);
+    if (ok) finish_strip<MV>(w, ep, u, red, s_inv, tid, kCThreads);
+    named_sync(kCThreads);
   }
 }
 
@@ -448,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nb = (int)(w.K >> 5);
-  const Sched sc = schedule<kRows>(w, (nb + CB - 1) / CB);
+  const Sched sc = make_sched(w.N, kRows, (nb + CB - 1) / CB, blockIdx.x, gridDim.x);
   float4 *xs = reinterpret_cast<float4 *>(ring + kStages * Gm::SB);  // [MV][nb][8], swizzled
   float *red = reinterpret_cast<float *>(xs + (size_t)MV * nb * 8);  // [64][MV]
 
@@ -579,7 +308,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           acc[r][m] = make_float2(0.0f, 0.0f);
         }
       named_sync(kCThreads);
-      finish_group<kRows, MV>(w, ep, scr, sc, g, red, nullptr, &s_last, ok);
+      finish_group<kRows, MV>(w, ep, scr, sc, g, red, nullptr, &s_last, ok, tid, kCThreads, 1);
       named_sync(kCThreads);
     }
     if (++c == sc.nc) {
@@ -593,11 +322,15 @@ __global__ void __launch_bounds__(kThreads, 2)
 // host side
 // ---------------------------------------------------------------------------
 size_t q4_smem(int64_t K, int MV) {
-  const int64_t nbx = ceil_div(K / 32, kQ4CB) * kQ4CB;
-  const int nm = (MV + 1) / 2;
-  (void)nm;
-  return 128 + (size_t)kQ4Stages * GeoQ4::SB + (size_t)nbx * 3 * MV * 4 * 8 + (size_t)4 * MV * nbx * 4 +
-         (size_t)MV * nbx * 4 + (size_t)kQ4Rows * MV * 4;
+  const int nbx = (int)q4_quads(K) * 4;
+  size_t xbytes = 0;
+  switch (MV) {
+    case 1: xbytes = Q4X<1>::bytes(nbx); break;
+    case 2: xbytes = Q4X<2>::bytes(nbx); break;
+    case 3: xbytes = Q4X<3>::bytes(nbx); break;
+    default: xbytes = Q4X<4>::bytes(nbx); break;
+  }
+  return 128 + (size_t)kQ4Stages * kQ4TileBytes + xbytes + (size_t)kGroupWarps * kQ4StripRows * MV * 4;
 }
 size_t q8_smem(int64_t K, int MV) {
   return 128 + (size_t)kStages * Geo<kRows, kTileBytes, 16>::SB + (size_t)MV * K * 4 + (size_t)kRows * MV * 4;
@@ -611,18 +344,22 @@ template <int MV>
 void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, float eps, bool do_norm,
                const Epilogue &ep, const GemvScratch &sc, int num_sms, cudaStream_t s) {
   const bool q4 = w.qtype == FG_Q4_0;
-  const int CB = q4 ? kQ4CB : 16, ROWS = q4 ? kQ4Rows : kRows, TB = q4 ? kQ4TB : kTileBytes;
-  const int64_t nb = w.K / 32, nc = ceil_div(nb, CB), G = ceil_div(w.N, ROWS), U = G * nc;
+  const int CB = 16, ROWS = kRows, TB = kTileBytes;  // Q8_0 tiles
+  // units: Q4_0 16-row strips; Q8_0 (32-row group, 16-block chunk) pairs
+  const int64_t nb = w.K / 32, nc = q4 ? 1 : ceil_div(nb, CB), G = q4 ? q4_strips(w.N) : ceil_div(w.N, ROWS);
+  const int64_t U = G * nc;
   FG_REQUIRE(U < (1ll << 31), FG_ERR_SHAPE, "gemv: matrix too large");
   const size_t smem = q4 ? q4_smem(w.K, MV) : q8_smem(w.K, MV);
   const int P = (int)std::min<int64_t>((smem <= kSmemTwo ? 2LL : 1LL) * num_sms, U);
-  int maxc = 1;
-  for (int64_t g = 0; g < G; ++g)
-    maxc = std::max(maxc, cta_of((int)(g * nc + nc - 1), (int)U, P) - cta_of((int)(g * nc), (int)U, P) + 1);
-  FG_REQUIRE((uint64_t)G * maxc * ROWS * MV <= sc.part_floats && G <= sc.n_tickets, FG_ERR_SHAPE,
-             "gemv: workspace too small for N=%lld K=%lld", (long long)w.N, (long long)w.K);
   GemvScratch scx = sc;
-  scx.maxc = maxc;
+  if (!q4) {  // stream-K fix-up slots of the Q8_0 kernel
+    int maxc = 1;
+    for (int64_t g = 0; g < G; ++g)
+      maxc = std::max(maxc, cta_of((int)(g * nc + nc - 1), (int)U, P) - cta_of((int)(g * nc), (int)U, P) + 1);
+    FG_REQUIRE((uint64_t)G * maxc * ROWS * MV <= sc.part_floats && G <= sc.n_tickets, FG_ERR_SHAPE,
+               "gemv: workspace too small for N=%lld K=%lld", (long long)w.N, (long long)w.K);
+    scx.maxc = maxc;
+  }
   static unsigned long long attr_set[2] = {0, 0};  // per instantiation, one bit per device
   int dev = 0;
   FG_CUDA(cudaGetDevice(&dev));

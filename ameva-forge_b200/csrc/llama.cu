@@ -21,11 +21,13 @@
 #include "nccl_dyn.cuh"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
 #include <string>
 
+#include "q4_gemv.cuh"
 #include "runtime.cuh"
 
 using namespace fg;
@@ -68,6 +70,8 @@ struct fg_llama {
   int host_pos = 0;
   int last_batch = 0;
   std::map<int, cudaGraphExec_t> graphs;
+  bool use_step = false;  // batch-1 decode runs the persistent step kernel
+  StepArgs step_args{};
 
   void *dalloc(uint64_t bytes) {
     void *p = ctx->alloc(bytes);
@@ -227,6 +231,59 @@ void read_logits(fg_llama *m, int B, float *host) {
 
 int set_err(int st, const char *msg);
 
+// State of the persistent decode-step kernel (decode_step.cu).
+void setup_step(fg_llama *m) {
+  Ctx &c = *m->ctx;
+  const int L = (int)m->layers.size(), d = m->d, G = m->Hq_l / m->Hkv_l;
+  std::vector<StepLayer> sl(L);
+  for (int l = 0; l < L; ++l) {
+    const LayerW &w = m->layers[l];
+    sl[l] = StepLayer{w.qkv, w.o, w.gateup, w.down, w.attn_norm, w.ffn_norm, w.k, w.v};
+  }
+  StepArgs &A = m->step_args;
+  A = StepArgs{};
+  StepLayer *dl = (StepLayer *)m->dalloc(sizeof(StepLayer) * std::max(L, 1));
+  if (L) c.h2d(dl, sl.data(), sizeof(StepLayer) * L);
+  const int P = decode_step_vctas(c.num_sms);
+  const int smax = std::max(1, P / m->Hkv_l);
+  A.attn_part = (float *)m->dalloc((uint64_t)m->Hkv_l * smax * G * (d + 2) * 4);
+  A.attn_cnt = (int *)m->dalloc((uint64_t)m->Hkv_l * 4);
+  FG_CUDA(cudaMemsetAsync(A.attn_cnt, 0, (uint64_t)m->Hkv_l * 4, c.stream));
+  A.bar = (unsigned long long *)m->dalloc(16);
+  FG_CUDA(cudaMemsetAsync(A.bar, 0, 16, c.stream));
+  A.argkey = (unsigned long long *)m->dalloc(8);
+  FG_CUDA(cudaMemsetAsync(A.argkey, 0, 8, c.stream));
+  A.layers = dl;
+  A.L = L;
+  A.lm_head = m->lm_head;
+  A.norm = m->norm;
+  A.embed = m->embed;
+  A.vocab = m->cfg.vocab_size;
+  A.H = m->H;
+  A.d = d;
+  A.Hq = m->Hq_l;
+  A.Hkv = m->Hkv_l;
+  A.I = m->I_l;
+  A.cap = m->cap;
+  A.eps = m->cfg.rms_norm_eps;
+  A.scale = (float)(1.0 / std::sqrt((double)d));
+  A.inv_freq = m->inv_freq;
+  A.h = m->h;
+  A.q = m->q;
+  A.att = m->att;
+  A.ffn = m->ffn;
+  A.logits = m->logits;
+  A.ids = m->ids;
+  A.pos = m->pos;
+  A.token_log = m->token_log;
+  A.step = m->step;
+  A.log_steps = m->log_steps;
+  A.gs = c.gemv;
+  A.err = c.gemv.err;
+  A.xarea_bytes = decode_step_xarea(d, G, m->H, m->I_l, (int64_t)m->Hq_l * d);
+  m->use_step = true;
+}
+
 }  // namespace
 
 extern "C" {
@@ -365,6 +422,12 @@ int fg_llama_create(fg_ctx *ctx_h, const fg_llama_config *cfg, fg_llama **out) {
     m->token_log = (int32_t *)m->dalloc((uint64_t)m->log_steps * m->max_batch * 4);
     m->step = (int *)m->dalloc(4);
     FG_CUDA(cudaMemsetAsync(m->step, 0, 4, c.stream));
+    // Batch-1 decode runs as one persistent kernel per token where it applies
+    // (FORGE_B200_DECODE=layered keeps the per-layer kernels, for comparison).
+    const char *mode = std::getenv("FORGE_B200_DECODE");
+    if (tp == 1 && !(mode && std::string(mode) == "layered") &&
+        decode_step_supported(d, m->Hq_l / m->Hkv_l, qt, H, m->I_l, (int64_t)m->Hq_l * d))
+      setup_step(m.get());
   } catch (...) {
     for (auto &p : m->allocs) c.free_async(p.first, p.second);
     throw;
@@ -480,6 +543,12 @@ int fg_llama_reset(fg_llama *m) {
   FG_LAPI_BEGIN
   LGuard g(m);
   FG_CUDA(cudaMemsetAsync(m->pos, 0, (uint64_t)m->max_batch * 4, m->ctx->stream));
+  if (m->use_step) {  // the step kernel's barrier, argmax and merge counters start over too
+    const StepArgs &A = m->step_args;
+    FG_CUDA(cudaMemsetAsync(A.bar, 0, 16, m->ctx->stream));
+    FG_CUDA(cudaMemsetAsync(A.argkey, 0, 8, m->ctx->stream));
+    FG_CUDA(cudaMemsetAsync(A.attn_cnt, 0, (uint64_t)A.Hkv * 4, m->ctx->stream));
+  }
   m->host_pos = 0;
   FG_LAPI_END
 }
@@ -522,7 +591,10 @@ static cudaGraphExec_t decode_graph(fg_llama *m, int B) {
   cudaGraph_t graph = nullptr;
   FG_CUDA(cudaStreamBeginCapture(c.stream, cudaStreamCaptureModeThreadLocal));
   try {
-    forward_tokens(m, B, 1, true);
+    if (B == 1 && m->use_step)
+      launch_decode_step(m->step_args, c.num_sms, c.stream);
+    else
+      forward_tokens(m, B, 1, true);
   } catch (...) {
     cudaStreamEndCapture(c.stream, &graph);
     if (graph) cudaGraphDestroy(graph);

@@ -148,6 +148,41 @@ int attn_decode_splits(const AttnArgs &a, int max_kv, int num_sms);
 uint64_t attn_decode_scratch_bytes(const AttnArgs &a, int splits);
 void launch_attention_decode(const AttnArgs &a, int splits, void *scratch, cudaStream_t s);
 
+// decode_step.cu: the persistent batch-1 decode step (one launch per token).
+struct StepLayer {
+  QMat qkv, o, gateup, down;
+  const float *attn_norm, *ffn_norm;
+  __half *k, *v;  // [Hkv][cap][d] fp16 (batch 1)
+};
+struct StepArgs {
+  const StepLayer *layers;  // [L], device memory
+  int L;
+  QMat lm_head;
+  const float *norm;
+  const __half *embed;      // [vocab][H]
+  int vocab, H, d, Hq, Hkv, I, cap;
+  float eps, scale;
+  const float *inv_freq;
+  float *h, *q, *att, *ffn, *logits;
+  int32_t *ids;             // [1] token in / out
+  int *pos;                 // [1] cache length
+  int32_t *token_log;
+  int *step;
+  int log_steps;
+  unsigned long long *argkey;  // 0 between launches
+  GemvScratch gs;              // error word
+  float *attn_part;            // [Hkv][2 SMs / Hkv][G][d + 2]
+  int *attn_cnt;               // [Hkv], 0 between launches
+  unsigned long long *bar;     // [2] grid barrier: arrivals, launches (never reset)
+  int *err;
+  uint64_t xarea_bytes;
+};
+bool decode_step_supported(int d, int G, int qtype, int64_t H, int64_t I, int64_t qdim);
+size_t decode_step_xarea(int d, int G, int64_t H, int64_t I, int64_t qdim);
+size_t decode_step_smem(int d, int G, int64_t H, int64_t I, int64_t qdim);
+int decode_step_vctas(int num_sms);
+void launch_decode_step(const StepArgs &A, int num_sms, cudaStream_t s);
+
 // misc.cu
 void launch_rmsnorm(const float *x, int64_t ldx, const float *gamma, float eps, int64_t tokens, int64_t dim,
                     float *out, cudaStream_t s);

@@ -8,7 +8,7 @@ namespace fg {
 
 // Error codes written to the device error word.
 enum DevErr { DEVERR_NONE = 0, DEVERR_GEMV_FULL = 1, DEVERR_GEMV_EMPTY = 2, DEVERR_ATTN_FULL = 3,
-              DEVERR_ATTN_EMPTY = 4, DEVERR_DRAIN = 5 };
+              DEVERR_ATTN_EMPTY = 4, DEVERR_DRAIN = 5, DEVERR_GRID = 6 };
 constexpr uint64_t kWaitTimeoutNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -77,6 +77,10 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 // Barrier among the first `threads` threads of the CTA (named barrier 1).
 __device__ __forceinline__ void named_sync(int threads) {
   asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+// Named barrier `id` (1..15) over `threads` threads (a multiple of 32).
+__device__ __forceinline__ void named_sync_id(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
 }  // namespace fg
