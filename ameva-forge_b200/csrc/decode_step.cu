@@ -167,15 +167,21 @@ constexpr int r4(int x) { return (x + 3) & ~3; }
 
 template <int D, int G>
 struct AttnCfg {
-  static constexpr int DC = D / 8;                             // dims per lane in q.k (8 lanes per key)
+  static constexpr int NS = 2;                                 // ring slots (32 keys each) per step
+  static constexpr int KEYS = NS * kKeysPerTile;               // keys per step
+  static constexpr int KW = KEYS / kGroupWarps;                // keys per warp in q.k (lanes: 4 keys x 8 dim chunks)
+  static constexpr int KR = KW / 4;                            // keys per lane in q.k
+  static constexpr int DC = D / 8;                             // dims per lane in q.k
   static constexpr int PAIRS = D / 2 * G;                      // (g, dim pair) outputs
   static constexpr int PPT = PAIRS > kGroupThreads ? PAIRS / kGroupThreads : 1;  // pairs per thread
-  static constexpr int KQ = PAIRS >= kGroupThreads ? 1 : kGroupThreads / PAIRS;   // key partitions
-  static constexpr int KPQ = kKeysPerTile / KQ;                // keys per partition
+  static constexpr int KQ = PAIRS >= kGroupThreads ? 1 : kGroupThreads / PAIRS;   // key partitions in p.V
+  static constexpr int KPQ = KEYS / KQ;                        // keys per partition
+  static constexpr int NCH = G * KEYS / 32;                    // 32-entry chunks of p
   static_assert(D == 64 || D == 128, "head_dim");
-  // shared scratch (floats): q [G][D], scores [G][32], p [G][32], warp max [8][G], psum [G], merge [KQ][G][D]
-  static constexpr int SM_Q = 0, SM_S = G * D, SM_P = SM_S + G * 32, SM_WM = SM_P + G * 32, SM_PS = SM_WM + 8 * G,
-                       SM_O = r4(SM_PS + G), SM_END = r4(SM_O + KQ * G * D);
+  // shared scratch (floats): q [G][D], scores [G][KEYS], p [G][KEYS], warp max [8][G], chunk sums [NCH],
+  // merge [KQ][G][D]
+  static constexpr int SM_Q = 0, SM_S = G * D, SM_P = SM_S + G * KEYS, SM_WM = SM_P + G * KEYS,
+                       SM_PS = SM_WM + 8 * G, SM_O = r4(SM_PS + NCH), SM_END = r4(SM_O + KQ * G * D);
 };
 
 template <int D, int G>
@@ -184,102 +190,133 @@ struct AttnState {
   float2 o[AttnCfg<D, G>::PPT];
 };
 
-// One tile of nk keys (K at kt, V at vt in shared memory) into the state.
+// One step of up to 64 keys: key j lives in row (j % 32) of slot (j / 32):
+// K rows at kt0 / kt1, V rows at vt0 / vt1 (shared memory); nk keys are valid
+// and rows past nk are never read.
 template <int D, int G>
-__device__ __forceinline__ void attn_tile(const __half *kt, const __half *vt, int nk, float *sm, AttnState<D, G> &S,
-                                          int tid, int bar) {
+__device__ __forceinline__ void attn_step(const __half *kt0, const __half *kt1, const __half *vt0, const __half *vt1,
+                                          int nk, float *sm, AttnState<D, G> &S, int tid, int bar) {
   using C = AttnCfg<D, G>;
   const int lane = tid & 31, warp = tid >> 5;
-  // ---- scores: warp w takes keys 4w..4w+3, lane (kk, c) dims [c DC, (c+1) DC)
+  // ---- scores: warp w takes keys [w KW, (w+1) KW); lane (kk, c): keys w KW + 4r + kk, dims [c DC, (c+1) DC)
   {
-    const int kk = lane >> 3, c = lane & 7, j = 4 * warp + kk;
-    float kf[C::DC];
-    const __half *kr = kt + j * D + c * C::DC;
+    const int kk = lane >> 3, c = lane & 7;
+    float kf[C::KR][C::DC];
 #pragma unroll
-    for (int v = 0; v < C::DC / 8; ++v) {
-      uint4 raw = make_uint4(0u, 0u, 0u, 0u);  // rows past nk are never read
-      if (j < nk) raw = *reinterpret_cast<const uint4 *>(kr + 8 * v);
-      const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+    for (int r = 0; r < C::KR; ++r) {
+      const int j = warp * C::KW + 4 * r + kk;
+      const __half *kr = (j < kKeysPerTile ? kt0 : kt1) + (j % kKeysPerTile) * D + c * C::DC;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float2 f = __half22float2(h2[e]);
-        kf[8 * v + 2 * e] = f.x;
-        kf[8 * v + 2 * e + 1] = f.y;
+      for (int v = 0; v < C::DC / 8; ++v) {
+        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+        if (j < nk) raw = *reinterpret_cast<const uint4 *>(kr + 8 * v);
+        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(h2[e]);
+          kf[r][8 * v + 2 * e] = f.x;
+          kf[r][8 * v + 2 * e + 1] = f.y;
+        }
       }
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float *qg = sm + C::SM_Q + g * D + c * C::DC;
-      float s = 0.0f;
+      float sa[C::KR], sb[C::KR];
+#pragma unroll
+      for (int r = 0; r < C::KR; ++r) sa[r] = sb[r] = 0.0f;
 #pragma unroll
       for (int e = 0; e < C::DC; e += 4) {
         const float4 q4 = *reinterpret_cast<const float4 *>(qg + e);
-        s = fmaf(q4.x, kf[e], s);
-        s = fmaf(q4.y, kf[e + 1], s);
-        s = fmaf(q4.z, kf[e + 2], s);
-        s = fmaf(q4.w, kf[e + 3], s);
+#pragma unroll
+        for (int r = 0; r < C::KR; ++r) {
+          sa[r] = fmaf(q4.x, kf[r][e], sa[r]);
+          sb[r] = fmaf(q4.y, kf[r][e + 1], sb[r]);
+          sa[r] = fmaf(q4.z, kf[r][e + 2], sa[r]);
+          sb[r] = fmaf(q4.w, kf[r][e + 3], sb[r]);
+        }
       }
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      s += __shfl_xor_sync(0xffffffffu, s, 4);
-      if (j >= nk) s = -INFINITY;
-      float wm = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, 8));
+      float wm = -INFINITY;
+#pragma unroll
+      for (int r = 0; r < C::KR; ++r) {
+        float sv = sa[r] + sb[r];
+        sv += __shfl_xor_sync(0xffffffffu, sv, 1);
+        sv += __shfl_xor_sync(0xffffffffu, sv, 2);
+        sv += __shfl_xor_sync(0xffffffffu, sv, 4);
+        const int j = warp * C::KW + 4 * r + kk;
+        if (j >= nk) sv = -INFINITY;
+        if (c == 0) sm[C::SM_S + g * C::KEYS + j] = sv;
+        wm = fmaxf(wm, sv);
+      }
+      wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 8));
       wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 16));
-      if (c == 0) sm[C::SM_S + g * 32 + j] = s;
       if (lane == 0) sm[C::SM_WM + warp * G + g] = wm;
     }
   }
   named_sync_id(bar, kGroupThreads);
-  // ---- new running max; p = exp(s - m') for (g, key) = (tid / 32, tid % 32)
+  // ---- new running max; p = exp(s - m') for entries (g, key); sums per 32-entry chunk
   float mnew[G], alpha[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     float tm = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) tm = fmaxf(tm, sm[C::SM_WM + w * G + g]);
+    for (int w = 0; w < kGroupWarps; ++w) tm = fmaxf(tm, sm[C::SM_WM + w * G + g]);
     mnew[g] = fmaxf(S.m[g], tm);
     alpha[g] = mnew[g] == -INFINITY ? 1.0f : expf(S.m[g] - mnew[g]);
   }
-  for (int idx = tid; idx < G * 32; idx += kGroupThreads) {
-    const int g = idx >> 5, j = idx & 31;
+  for (int idx = tid; idx < G * C::KEYS; idx += kGroupThreads) {
+    const int g = idx / C::KEYS;
     float mg = -INFINITY;
 #pragma unroll
     for (int gg = 0; gg < G; ++gg)
       if (gg == g) mg = mnew[gg];
-    const float s = sm[C::SM_S + g * 32 + j];
-    const float p = s == -INFINITY ? 0.0f : expf(s - mg);
-    sm[C::SM_P + g * 32 + j] = p;
-    const float ps = warp_sum(p);
-    if (j == 0) sm[C::SM_PS + g] = ps;
+    const float sv = sm[C::SM_S + idx];
+    const float p = sv == -INFINITY ? 0.0f : expf(sv - mg);
+    sm[C::SM_P + idx] = p;
+    const float ps = warp_sum(p);  // the warp's 32 entries share g (KEYS is a multiple of 32)
+    if ((idx & 31) == 0) sm[C::SM_PS + (idx >> 5)] = ps;
   }
   named_sync_id(bar, kGroupThreads);
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    S.l[g] = S.l[g] * alpha[g] + sm[C::SM_PS + g];
+    float ps = 0.0f;
+#pragma unroll
+    for (int ch = 0; ch < C::KEYS / 32; ++ch) ps += sm[C::SM_PS + g * (C::KEYS / 32) + ch];
+    S.l[g] = S.l[g] * alpha[g] + ps;
     S.m[g] = mnew[g];
   }
   // ---- o += p V: thread -> (pair slot, key partition kq)
   const int slot = tid % (C::PAIRS / C::PPT), kq = tid / (C::PAIRS / C::PPT);
+  const int kbeg = kq * C::KPQ, kend = min(kbeg + C::KPQ, nk);
 #pragma unroll
   for (int r = 0; r < C::PPT; ++r) {
-    const int pr = slot * C::PPT + r;       // (g, dim pair) index
+    const int pr = slot * C::PPT + r;  // (g, dim pair) index
     const int g = pr / (D / 2), dp = pr % (D / 2);
     float a = 1.0f;
 #pragma unroll
     for (int gg = 0; gg < G; ++gg)
       if (gg == g) a = alpha[gg];
-    float2 o = make_float2(S.o[r].x * a, S.o[r].y * a);
-    const float *pg = sm + C::SM_P + g * 32 + kq * C::KPQ;
-    const __half2 *vr = reinterpret_cast<const __half2 *>(vt + (kq * C::KPQ) * D) + dp;
-    const int kend = min(C::KPQ, nk - kq * C::KPQ);  // rows past nk are never read
-#pragma unroll 8
-    for (int j = 0; j < kend; ++j) {
-      const float p = pg[j];
-      const float2 v = __half22float2(vr[j * (D / 2)]);
-      o.x = fmaf(p, v.x, o.x);
-      o.y = fmaf(p, v.y, o.y);
+    const float *pg = sm + C::SM_P + g * C::KEYS;
+    float2 o0 = make_float2(S.o[r].x * a, S.o[r].y * a), o1 = make_float2(0.0f, 0.0f);
+    int j = kbeg;
+    for (; j + 1 < kend; j += 2) {
+      const float2 v0 =
+          __half22float2(reinterpret_cast<const __half2 *>((j < kKeysPerTile ? vt0 : vt1) + (j % kKeysPerTile) * D)[dp]);
+      const float2 v1 = __half22float2(
+          reinterpret_cast<const __half2 *>((j + 1 < kKeysPerTile ? vt0 : vt1) + ((j + 1) % kKeysPerTile) * D)[dp]);
+      const float p0 = pg[j], p1 = pg[j + 1];
+      o0.x = fmaf(p0, v0.x, o0.x);
+      o0.y = fmaf(p0, v0.y, o0.y);
+      o1.x = fmaf(p1, v1.x, o1.x);
+      o1.y = fmaf(p1, v1.y, o1.y);
     }
-    S.o[r] = o;
+    if (j < kend) {
+      const float2 v0 =
+          __half22float2(reinterpret_cast<const __half2 *>((j < kKeysPerTile ? vt0 : vt1) + (j % kKeysPerTile) * D)[dp]);
+      o0.x = fmaf(pg[j], v0.x, o0.x);
+      o0.y = fmaf(pg[j], v0.y, o0.y);
+    }
+    S.o[r] = make_float2(o0.x + o1.x, o0.y + o1.y);
   }
 }
 
@@ -401,15 +438,22 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
 #pragma unroll
         for (int r = 0; r < Cf::PPT; ++r) st.o[r] = make_float2(0.0f, 0.0f);
         named_sync_id(gbar, kGroupThreads);
-        for (int t = t0; t < t1; ++t, ++i) {
-          const int sl = i % kStepStages;
-          ok = ok && mbar_wait(&fl[sl], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
-          // every thread runs the tile (it holds group barriers); without data it takes no keys
-          const __half *kt = reinterpret_cast<const __half *>(ring + sl * kQ4TileBytes);
-          attn_tile<D, G>(kt, kt + kKeysPerTile * D, ok ? min(kKeysPerTile, npos - t * kKeysPerTile) : 0, sm, st,
-                          gtid, gbar);
+        for (int t = t0; t < t1; t += Cf::NS) {  // two ring slots (64 keys) per step
+          const int ns = min(Cf::NS, t1 - t);
+          const int sl0 = i % kStepStages, sl1 = (i + 1) % kStepStages;
+          ok = ok && mbar_wait(&fl[sl0], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
+          if (ns == 2) ok = ok && mbar_wait(&fl[sl1], (uint32_t)((i + 1) / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
+          const __half *k0 = reinterpret_cast<const __half *>(ring + sl0 * kQ4TileBytes);
+          const __half *k1 = ns == 2 ? reinterpret_cast<const __half *>(ring + sl1 * kQ4TileBytes) : k0;
+          // every thread runs the step (it holds group barriers); without data it takes no keys
+          attn_step<D, G>(k0, k1, k0 + kKeysPerTile * D, k1 + kKeysPerTile * D,
+                          ok ? min(ns * kKeysPerTile, npos - t * kKeysPerTile) : 0, sm, st, gtid, gbar);
           __syncwarp();
-          if (lane == 0) mbar_arrive(&em[sl]);
+          if (lane == 0) {
+            mbar_arrive(&em[sl0]);
+            if (ns == 2) mbar_arrive(&em[sl1]);
+          }
+          i += ns;
         }
         if (last) {
           // key npos (this step's K/V) from global memory into a one-key tile
@@ -422,7 +466,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
             kt[D + e] = __ldcg(vg + e);
           }
           named_sync_id(gbar, kGroupThreads);
-          attn_tile<D, G>(kt, kt + D, ok ? 1 : 0, sm, st, gtid, gbar);
+          attn_step<D, G>(kt, kt, kt + D, kt + D, ok ? 1 : 0, sm, st, gtid, gbar);
         }
         // ---- combine the key partitions, write the unit's partial
         float *om = sm + Cf::SM_O;  // [KQ][G][D]
