@@ -11,9 +11,13 @@ step is fixed (strong scaling).  A step = one decode token of every sequence.
            on the library's stream, max over ranks;
   e2e    : the same metric through the public C ABI call (fg_llama_decode) with
            host buffers: each step copies the input id in and the next id out;
-  roofline: the fused dequant-GEMV (the dominant kernel) re-timed live on the
-           7B layer shapes with cold L2, algorithmic bytes / launch time vs the
-           measured HBM copy bandwidth;
+  roofline: the dominant kernel.  On one GPU a decode step is one launch of
+           the persistent decode-step kernel (k_decode_step), so its
+           algorithmic bytes per launch (all Q4_0 weights + the KV cache read
+           at the mean timed position + norms and vectors) / its time per
+           launch vs the measured HBM copy bandwidth.  Under tensor parallelism
+           the dominant kernel is the fused dequant-GEMV, re-timed live on the
+           rank's 7B layer shapes with cold L2;
   cpu_baseline: the CPU oracle (a port of the reference arithmetic) decoding
            a bounded sample of the same workload on the host cores.
 
@@ -52,6 +56,9 @@ def parse():
     ap.add_argument("--cpu-baseline", type=int, default=1, help="time the CPU oracle sample (rank 0, N=1)")
     ap.add_argument("--roofline-only", action="store_true",
                     help="only time the dequant-GEMV on the layer shapes (the profiling case)")
+    ap.add_argument("--profile-layers", type=int, default=0,
+                    help="profiling case: a model of this many 7B layers at context 4096, `steps` decode steps; "
+                         "prints no bench line")
     return ap.parse_args()
 
 
@@ -236,14 +243,62 @@ def measured_peak():
         return 6650.0, "fallback"
 
 
+def q4_bytes(n, k):
+    return n * (k // 32) * 18
+
+
+def step_bytes(layers, pos_mean, world=1):
+    """Algorithmic DRAM bytes of one batch-1 decode step (this rank's shard):
+    every Q4_0 weight once, the fp16 KV cache of keys [0, pos] read once and
+    the new key/value written, the norms, the embedding row and the
+    activation vectors (each GEMV's input and output once)."""
+    H, I, d = SHAPE["hidden_size"], SHAPE["intermediate_size"] // world, H_D
+    hq, hkv, V = SHAPE["num_attention_heads"] // world, SHAPE["num_key_value_heads"] // world, SHAPE["vocab_size"] // world
+    gemvs = [((hq + 2 * hkv) * d, H), (H, hq * d), (2 * I, H), (H, I)]
+    per_layer = sum(q4_bytes(n, k) + 4 * (n + k) for n, k in gemvs)
+    per_layer += 2 * H * 4                          # attn / ffn norm weights
+    per_layer += 2 * hkv * d * 2 * (pos_mean + 1)   # K and V of keys [0, pos]
+    per_layer += 2 * hkv * d * 2                    # the new key / value
+    head = q4_bytes(V, H) + 4 * (V + H) + H * 4 + H * 2
+    return layers * per_layer + head
+
+
+H_D = 128
+
+
 def ncu_traffic():
-    """dram bytes per GEMV launch from the committed ncu summary, if any."""
-    p = os.path.join(REPO, "profiles", "qgemv_q4_0_traffic.json")
+    """DRAM bytes per decode-step launch from the committed ncu summary, if any."""
+    p = os.path.join(REPO, "profiles", "decode_step_7b_traffic.json")
     try:
         with open(p) as f:
             return json.load(f)
     except (OSError, ValueError):
         return None
+
+
+def profile_case(args, local):
+    """A 7B-shaped model of --profile-layers layers at context 4096: W + K
+    decode steps through the same graph as the bench (for ncu captures of the
+    decode-step kernel on a case that holds well under a GB on the device)."""
+    import forge_b200
+    ctx = forge_b200.Context(device=local)
+    L = args.profile_layers
+    shape = {**SHAPE, "num_hidden_layers": L}
+    cap = CONTEXT + args.warmup + args.steps + 8
+    model = forge_b200.LlamaForCausalLM(forge_b200.LlamaConfig(max_position_embeddings=cap, max_batch=1, qtype="Q4_0",
+                                                               **shape), ctx)
+    model.synthesize(SEED)
+    prompt = np.random.default_rng(SEED).integers(0, SHAPE["vocab_size"], (1, CONTEXT), dtype=np.int32)
+    model.forward(prompt, return_logits=False)
+    model.generate_device(1, args.warmup + args.steps)
+    ctx.synchronize()
+    pos_mean = CONTEXT + args.warmup + (args.steps - 1) / 2.0
+    print(json.dumps({"profile_case": f"{L} of 32 Llama-2-7B layers, context {CONTEXT}, batch 1",
+                      "decode_steps": args.warmup + args.steps, "first_profiled_launch": args.warmup,
+                      "algorithmic_bytes_per_launch": step_bytes(L, pos_mean),
+                      "full_model_bytes_per_launch": step_bytes(SHAPE["num_hidden_layers"], pos_mean)}), flush=True)
+    model.close()
+    ctx.shutdown()
 
 
 def main():
@@ -268,6 +323,9 @@ def main():
         print(json.dumps({"kernel": "k_qgemv", "GBps": b_launch / (ms_launch / 1e3) / 1e9, "peak": peak,
                           "per_shape": per_shape}), flush=True)
         ctx.shutdown()
+        return
+    if args.profile_layers:
+        profile_case(args, local)
         return
     nid = None
     if world > 1:
@@ -336,8 +394,23 @@ def main():
     # ---- roofline of the dominant kernel ----
     b_launch, ms_launch, per_shape = gemv_roofline(ctx, world)
     peak, peak_kind = measured_peak()
-    achieved = b_launch / (ms_launch / 1e3) / 1e9
-    traffic = ncu_traffic()
+    step_kernel = world == 1 and os.environ.get("FORGE_B200_DECODE", "") != "layered"
+    pos_mean = CONTEXT + args.warmup + (args.steps - 1) / 2.0
+    if step_kernel:
+        alg = step_bytes(SHAPE["num_hidden_layers"], pos_mean)
+        roof = {"bound": "hbm", "kernel": "k_decode_step (persistent decode step: Q4_0 GEMVs + split-KV attention)",
+                "achieved": alg / (ms / args.steps / 1e3) / 1e9, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "algorithmic_bytes_per_launch": alg, "us_per_launch": 1e3 * ms / args.steps,
+                "launches_per_step": 1,
+                "gemv_alone": {"GBps": b_launch / (ms_launch / 1e3) / 1e9, "per_shape": per_shape}}
+    else:
+        roof = {"bound": "hbm", "kernel": "k_qgemv (fused Q4_0 dequant-GEMV)",
+                "achieved": b_launch / (ms_launch / 1e3) / 1e9, "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                "algorithmic_bytes_per_launch": b_launch, "us_per_launch": ms_launch * 1e3, "per_shape": per_shape}
+    roof["frac"] = roof["achieved"] / peak
+    traffic = ncu_traffic() if step_kernel else None
+    # ncu dram bytes per launch: measured on a 2-layer launch, scaled by the bytes streamed
+    roof["traffic"] = traffic["traffic_over_algorithmic"] * roof["algorithmic_bytes_per_launch"] if traffic else None
 
     model.close()
     ctx.shutdown()
@@ -346,18 +419,15 @@ def main():
         cpu = cpu_sample()
     if rank == 0:
         L = SHAPE["num_hidden_layers"]
-        launches = (5 * L + 4 + (1 if world > 1 else 0)) * args.steps
+        launches = args.steps if step_kernel else (5 * L + 4 + (3 if world > 1 else 0)) * args.steps
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "fp32", "data": "synthetic", "config": config_block(world),
+            "vs_baseline": None, "dtype": "q4_0 x int8-digit MMA, fp32 accumulate", "data": "synthetic",
+            "config": config_block(world),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": 4 * BATCH,
                     "d2h_bytes_per_step": 4 * BATCH},
-            "roofline": {"bound": "hbm", "kernel": "k_qgemv (fused Q4_0 dequant-GEMV)", "achieved": achieved,
-                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
-                         "traffic": traffic.get("bytes_per_launch") if traffic else None,
-                         "algorithmic_bytes_per_launch": b_launch, "us_per_launch": ms_launch * 1e3,
-                         "per_shape": per_shape},
+            "roofline": roof,
             "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
             "setup": {"synthesize_s": t_synth, "prefill_s": t_prefill, "prefill_tokens": CONTEXT * BATCH},
         }
