@@ -559,7 +559,7 @@ void qmatmul_launch(Ctx &c, const Tensor &xt, const QMat &q, int64_t M, float *y
   if (gemv_supported(q, (int)M))
     launch_qgemv_ld(q, (const float *)xt.ptr, (int)M, q.K, nullptr, 0.0f, false, ep, c.gemv, c.num_sms, c.stream);
   else
-    launch_qgemm(q, (const float *)xt.ptr, (int)M, q.K, ep, c.num_sms, c.stream);
+    launch_qgemm(q, (const float *)xt.ptr, (int)M, q.K, ep, c.gemv, c.num_sms, c.stream);
 }
 }  // namespace
 

@@ -6,6 +6,9 @@
 // reference unpack ((code - zero) * scale) into shared memory and consumed by
 // a 4x4 register tile per thread.  It is the portable GEMM of this library;
 // the tensor-core GEMM (gemm_tc.cu) takes the shapes it supports.
+#include <cstdlib>
+#include <string>
+
 #include "epilogue.cuh"
 
 namespace fg {
@@ -138,9 +141,18 @@ __global__ void __launch_bounds__(256) k_matmul_f32(const float *__restrict__ A,
 
 }  // namespace
 
-void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, int num_sms, cudaStream_t s) {
-  (void)num_sms;
+void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, const GemvScratch &sc,
+                  int num_sms, cudaStream_t s) {
   if (M == 0 || w.N == 0) return;
+  // Q4_0 runs on the tensor cores; FORGE_B200_GEMM=simt keeps the CUDA-core kernel (for comparison)
+  static const bool force_simt = [] {
+    const char *e = std::getenv("FORGE_B200_GEMM");
+    return e && std::string(e) == "simt";
+  }();
+  if (!force_simt && qgemm_tc_supported(w, M)) {
+    launch_qgemm_tc(w, x, M, ldx, ep, sc, num_sms, s);
+    return;
+  }
   dim3 grid((unsigned)ceil_div(w.N, BN), (unsigned)ceil_div(M, BM));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;

@@ -112,7 +112,7 @@ void linear(fg_llama *m, const QMat &w, const float *x, int M, int64_t ldx, cons
       xx = m->xn;
       ld = w.K;
     }
-    launch_qgemm(w, xx, M, ld, ep, c.num_sms, c.stream);
+    launch_qgemm(w, xx, M, ld, ep, c.gemv, c.num_sms, c.stream);
   }
 }
 

@@ -118,7 +118,12 @@ bool gemv_supported(const QMat &w, int M);
 void launch_qgemv_ld(const QMat &w, const float *x, int M, int64_t ldx, const float *norm_gamma, float norm_eps,
                      bool do_norm, const Epilogue &ep, const GemvScratch &sc, int num_sms, cudaStream_t s);
 // gemm.cu: the same contract without the fused norm, any M (prefill / batched decode).
-void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, int num_sms, cudaStream_t s);
+void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, const GemvScratch &sc,
+                  int num_sms, cudaStream_t s);
+// gemm_tc.cu: the Q4_0 GEMM on tcgen05 tensor cores (launch_qgemm picks it).
+bool qgemm_tc_supported(const QMat &w, int M);
+void launch_qgemm_tc(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, const GemvScratch &sc,
+                     int num_sms, cudaStream_t s);
 void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s);
 
 // attention.cu

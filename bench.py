@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--cpu-baseline", type=int, default=1, help="time the CPU oracle sample (rank 0, N=1)")
     ap.add_argument("--roofline-only", action="store_true",
                     help="only time the dequant-GEMV on the layer shapes (the profiling case)")
+    ap.add_argument("--gemm-table", action="store_true",
+                    help="the Q4_0 dequant-GEMV/GEMM table: 4096x11008 and 11008x4096 at batch 1/8/32/128")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="profiling case: a model of this many 7B layers at context 4096, `steps` decode steps; "
                          "prints no bench line")
@@ -227,6 +229,51 @@ def gemv_roofline(ctx, world, reps=8, rounds=10):
     return total_bytes / launches, total_ms / launches, per_shape
 
 
+def gemm_table(ctx, reps=8, rounds=10):
+    """Q4_0 dequant-GEMV/GEMM of the scope table: W [N, K] in {4096 x 11008,
+    11008 x 4096} from N(0, 0.02), x ~ N(0, 1) at batch 1/8/32/128.  Cold L2:
+    every replay rotates over `reps` weight copies (8 x 25.4 MB > 2 x L2).
+    Graph-captured launches on the library stream, CUDA-event timed."""
+    stream = torch.cuda.ExternalStream(ctx.stream_ptr())
+    peak_bw, _ = measured_peak()
+    with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+        peak_tf = float(json.load(f).get("bf16_tflops", 1590.0))
+    rows = []
+    for (N, K) in [(4096, 11008), (11008, 4096)]:
+        ws = [ctx.synth_quant("Q4_0", N, K, seed=77 + r, std=0.02) for r in range(reps)]
+        for M in (1, 8, 32, 128):
+            x = ctx.synth_normal((M, K), np.float32, seed=K + M)
+            out = ctx.empty((M, N), np.float32)
+            for w in ws:
+                ctx.qmatmul_into(x, w, out)
+            ctx.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for w in ws:
+                    ctx.qmatmul_into(x, w, out)
+            with torch.cuda.stream(stream):
+                g.replay()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(rounds):
+                    g.replay()
+                e1.record()
+            e1.synchronize()
+            us = 1000 * e0.elapsed_time(e1) / (rounds * reps)
+            byt = N * (K // 32) * 18 + 4 * M * (K + N)
+            fl = 2.0 * M * N * K
+            rows.append({"N": N, "K": K, "batch": M, "kernel": "k_qgemv" if M <= 4 else "k_qgemm_tc (tcgen05)",
+                         "us": us, "GBps": byt / us / 1e3, "TFLOPs": fl / us / 1e6,
+                         "hbm_frac": byt / us / 1e3 / peak_bw, "tensor_frac": fl / us / 1e6 / peak_tf})
+            del g
+            ctx.dispose(x)
+            ctx.dispose(out)
+        for w in ws:
+            ctx.dispose(w)
+        ctx.synchronize()
+    return rows
+
+
 def ctx_stream(ctx):
     import ctypes
     from forge_b200 import _capi as C
@@ -316,6 +363,12 @@ def main():
         return
 
     import forge_b200
+    if args.gemm_table:
+        ctx = forge_b200.Context(device=local)
+        for r in gemm_table(ctx):
+            print(json.dumps(r), flush=True)
+        ctx.shutdown()
+        return
     if args.roofline_only:
         ctx = forge_b200.Context(device=local)
         b_launch, ms_launch, per_shape = gemv_roofline(ctx, world)
