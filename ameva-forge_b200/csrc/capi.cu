@@ -131,6 +131,20 @@ void Ctx::sync() {
   check_device_error();
 }
 
+void Ctx::ensure_xh(uint64_t elems) {
+  if (elems <= gemv.xh_elems) return;
+  cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+  FG_CUDA(cudaStreamIsCapturing(stream, &st));
+  FG_REQUIRE(st == cudaStreamCaptureStatusNone, FG_ERR_VALIDATION,
+             "GEMM activation scratch must grow outside stream capture (run the shape once before capturing)");
+  if (gemv.xh) free_async(gemv.xh, gemv.xh_elems * 2);
+  gemv.xh = nullptr;
+  gemv.xh_elems = 0;
+  const uint64_t n = align_up(elems, 1u << 16);
+  gemv.xh = (__half *)alloc(n * 2);
+  gemv.xh_elems = n;
+}
+
 void Ctx::check_device_error() {
   if (!gemv.err) return;
   int e = 0;
@@ -333,6 +347,7 @@ int fg_shutdown(fg_ctx *ctx) {
     cudaStreamSynchronize(c.stream);
     for (auto &kv : c.tensors) cudaFreeAsync(kv.second.ptr, c.stream);
     if (c.gemv.part) cudaFreeAsync(c.gemv.part, c.stream);
+    if (c.gemv.xh) cudaFreeAsync(c.gemv.xh, c.stream);
     c.tensors.clear();
     auto it = g_rope.find(&c);
     if (it != g_rope.end()) {
@@ -558,8 +573,10 @@ void qmatmul_launch(Ctx &c, const Tensor &xt, const QMat &q, int64_t M, float *y
   if (M == 0 || q.N == 0) return;
   if (gemv_supported(q, (int)M))
     launch_qgemv_ld(q, (const float *)xt.ptr, (int)M, q.K, nullptr, 0.0f, false, ep, c.gemv, c.num_sms, c.stream);
-  else
+  else {
+    if (qgemm_tc_supported(q, (int)M)) c.ensure_xh(tc_xh_elems(M, q.K));
     launch_qgemm(q, (const float *)xt.ptr, (int)M, q.K, ep, c.gemv, c.num_sms, c.stream);
+  }
 }
 }  // namespace
 

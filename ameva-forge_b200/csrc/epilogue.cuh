@@ -66,4 +66,30 @@ __device__ inline void epi_store_one(const Epilogue &ep, int64_t n, int m, float
   *y = v;
 }
 
+// Four consecutive columns n..n+3 (n even) of token m, of a matrix with N
+// columns: one 16-byte store where the row allows it, else two pairs (and a
+// single column at an odd end, PLAIN only).
+__device__ inline void epi_store_quad(const Epilogue &ep, int64_t n, int64_t N, int m, float4 v) {
+  if (ep.mode == EPI_PLAIN && n + 3 < N) {
+    float *y = ep.y + (int64_t)m * ep.ldy + n;
+    const float *r = ep.resid ? ep.resid + (int64_t)m * ep.ldy + n : nullptr;
+    if ((((uintptr_t)y | (uintptr_t)r) & 15) == 0) {
+      if (r) {
+        const float4 a = __ldcg(reinterpret_cast<const float4 *>(r));
+        v = make_float4(__fadd_rn(a.x, v.x), __fadd_rn(a.y, v.y), __fadd_rn(a.z, v.z), __fadd_rn(a.w, v.w));
+      }
+      *reinterpret_cast<float4 *>(y) = v;
+      return;
+    }
+  }
+  const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int k = 0; k < 4; k += 2) {
+    if (n + k + 1 < N)
+      epi_store_pair(ep, n + k, m, e[k], e[k + 1]);
+    else if (n + k < N && ep.mode == EPI_PLAIN)
+      epi_store_one(ep, n + k, m, e[k]);
+  }
+}
+
 }  // namespace fg

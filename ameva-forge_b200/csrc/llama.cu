@@ -422,6 +422,8 @@ int fg_llama_create(fg_ctx *ctx_h, const fg_llama_config *cfg, fg_llama **out) {
     m->token_log = (int32_t *)m->dalloc((uint64_t)m->log_steps * m->max_batch * 4);
     m->step = (int *)m->dalloc(4);
     FG_CUDA(cudaMemsetAsync(m->step, 0, 4, c.stream));
+    // fp16 activations of the tensor-core GEMM, sized for the largest prefill chunk
+    c.ensure_xh(tc_xh_elems(m->m_max, std::max(std::max(H, m->I_l), m->Hq_l * d)));
     // Batch-1 decode runs as one persistent kernel per token where it applies
     // (FORGE_B200_DECODE=layered keeps the per-layer kernels, for comparison).
     const char *mode = std::getenv("FORGE_B200_DECODE");

@@ -37,6 +37,8 @@ struct GemvScratch {
   int64_t n_tickets = 0;
   int *err = nullptr;
   int maxc = 1;
+  __half *xh = nullptr;  // fp16 copy of a GEMM's activations (tensor-core GEMM B operand)
+  uint64_t xh_elems = 0;
 };
 
 // One context = one device, one stream, one handle namespace (the reference's
@@ -74,6 +76,7 @@ struct Ctx {
   void d2h(void *dst, const void *src, uint64_t bytes);
   void sync();
   void check_device_error();  // raises if a kernel's bounded wait timed out
+  void ensure_xh(uint64_t elems);  // grow gemv.xh (never during stream capture)
 };
 
 uint64_t dtype_bytes(int dtype, int64_t numel, const int64_t *shape, int ndim);
@@ -122,6 +125,9 @@ void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilo
                   int num_sms, cudaStream_t s);
 // gemm_tc.cu: the Q4_0 GEMM on tcgen05 tensor cores (launch_qgemm picks it).
 bool qgemm_tc_supported(const QMat &w, int M);
+// fp16 scratch elements the tensor-core GEMM needs for M tokens of K columns
+// (rows padded to whole 128-column quads).
+inline uint64_t tc_xh_elems(int64_t M, int64_t K) { return (uint64_t)M * (uint64_t)(q4_quads(K) * 128); }
 void launch_qgemm_tc(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, const GemvScratch &sc,
                      int num_sms, cudaStream_t s);
 void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s);

@@ -59,9 +59,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
   }
 }
 
+// Wait for a phase during a drain: bounded by time only (a drain must wait
+// for copies in flight even after another thread reported an error).
+__device__ __forceinline__ void mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+  const uint64_t t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kWaitTimeoutNs) return;
+}
+
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
 }
 

@@ -24,7 +24,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }  // namespace
 
 CUtensorMap make_tmap_2d(const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t rows, uint64_t cols,
-                         uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols) {
+                         uint64_t pitch_bytes, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swizzle) {
   FG_REQUIRE(((uintptr_t)base & 15) == 0 && pitch_bytes % 16 == 0 && (box_cols * elem_bytes) % 16 == 0 &&
                  box_rows >= 1 && box_rows <= 256 && box_cols >= 1 && box_cols <= 256,
              FG_ERR_VALIDATION, "tensor map: misaligned base/pitch/box");
@@ -34,7 +34,25 @@ CUtensorMap make_tmap_2d(const void *base, CUtensorMapDataType dtype, int elem_b
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_fn()(&m, dtype, 2, const_cast<void *>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FG_REQUIRE(r == CUDA_SUCCESS, FG_ERR_INTERNAL_GPU, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return m;
+}
+
+CUtensorMap make_tmap_3d(const void *base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0, uint64_t d1,
+                         uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2,
+                         CUtensorMapSwizzle swizzle) {
+  FG_REQUIRE(((uintptr_t)base & 15) == 0 && s1 % 16 == 0 && s2 % 16 == 0 && (b0 * elem_bytes) % 16 == 0 &&
+                 b0 >= 1 && b0 <= 256 && b1 >= 1 && b1 <= 256 && b2 >= 1 && b2 <= 256,
+             FG_ERR_VALIDATION, "tensor map: misaligned base/stride/box");
+  CUtensorMap m;
+  const cuuint64_t dims[3] = {d0, d1, d2};
+  const cuuint64_t strides[2] = {s1, s2};
+  const cuuint32_t box[3] = {b0, b1, b2};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, dtype, 3, const_cast<void *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   FG_REQUIRE(r == CUDA_SUCCESS, FG_ERR_INTERNAL_GPU, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return m;
