@@ -439,6 +439,10 @@ void launch_attention(const AttnArgs &a, int num_sms, cudaStream_t s) {
   FG_REQUIRE(a.d >= 1 && a.d <= 256, FG_ERR_SHAPE, "HeadDim %d exceeds max supported dimension 256", a.d);
   FG_REQUIRE(a.H % a.Hkv == 0, FG_ERR_SHAPE, "Query heads %d must be divisible by KV heads %d", a.H, a.Hkv);
   if (a.B == 0 || a.Nq == 0 || a.H == 0) return;
+  if (a.Nq >= 16 && attn_tc_supported(a)) {  // prefill: tensor cores (fewer query rows use the SIMT tile)
+    launch_attention_tc(a, s);
+    return;
+  }
   if (a.d <= 64)
     launch_simt_t<64, 32>(a, s);
   else if (a.d <= 128)

@@ -143,6 +143,7 @@ AttnArgs attn_args(fg_llama *m, const LayerW &L, int B, int T) {
   a.scale = (float)(1.0 / std::sqrt((double)m->d));
   a.causal = 1;
   a.scratch_batch = m->max_batch;
+  a.err = m->ctx->gemv.err;
   return a;
 }
 
@@ -392,6 +393,9 @@ int fg_llama_create(fg_ctx *ctx_h, const fg_llama_config *cfg, fg_llama **out) {
       w.down = make_qmat(m.get(), qt, H, m->I_l);
       w.k = (__half *)m->dalloc(kv_elems * 2);
       w.v = (__half *)m->dalloc(kv_elems * 2);
+      // finite past the live length: the tensor-core attention reads whole 128-key blocks (masked)
+      FG_CUDA(cudaMemsetAsync(w.k, 0, kv_elems * 2, c.stream));
+      FG_CUDA(cudaMemsetAsync(w.v, 0, kv_elems * 2, c.stream));
     }
     std::vector<float> inv(d / 2);
     for (int p = 0; p < d / 2; ++p) inv[p] = (float)std::pow((double)k.rope_theta, -2.0 * (double)p / (double)d);

@@ -148,8 +148,15 @@ struct AttnArgs {
   float scale = 1.0f;
   int causal = 0;
   int scratch_batch = 0;                 // decode scratch was sized for this batch (0 = B)
+  int *err = nullptr;                    // device error word of bounded waits (tensor-core path)
 };
 void launch_attention(const AttnArgs &a, int num_sms, cudaStream_t s);
+// attention_tc.cu: tcgen05 flash attention (fp16 K/V, head_dim 64 or 128,
+// 16-byte aligned rows).  K/V past the live length up to the cache extent
+// (kv_sh / d tokens) are read in whole 128-key blocks and masked, so they must
+// hold finite values.
+bool attn_tc_supported(const AttnArgs &a);
+void launch_attention_tc(const AttnArgs &a, cudaStream_t s);
 bool attn_decode_supported(const AttnArgs &a);
 // Split-KV decode attention (Nq == 1, fp16 cache, fp32 q).  Needs a scratch
 // area of attn_decode_scratch_bytes() bytes: per-head arrival counters first

@@ -58,4 +58,21 @@ CUtensorMap make_tmap_3d(const void *base, CUtensorMapDataType dtype, int elem_b
   return m;
 }
 
+CUtensorMap make_tmap_4d(const void *base, CUtensorMapDataType dtype, int elem_bytes, const uint64_t (&dims)[4],
+                         const uint64_t (&strides)[3], const uint32_t (&box)[4], CUtensorMapSwizzle swizzle) {
+  bool ok = ((uintptr_t)base & 15) == 0 && (box[0] * elem_bytes) % 16 == 0;
+  for (int i = 0; i < 3; ++i) ok = ok && strides[i] % 16 == 0;
+  for (int i = 0; i < 4; ++i) ok = ok && box[i] >= 1 && box[i] <= 256 && dims[i] >= 1;
+  FG_REQUIRE(ok, FG_ERR_VALIDATION, "tensor map: misaligned base/stride/box");
+  CUtensorMap m;
+  const cuuint64_t d[4] = {dims[0], dims[1], dims[2], dims[3]};
+  const cuuint64_t st[3] = {strides[0], strides[1], strides[2]};
+  const cuuint32_t bx[4] = {box[0], box[1], box[2], box[3]};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = encode_fn()(&m, dtype, 4, const_cast<void *>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FG_REQUIRE(r == CUDA_SUCCESS, FG_ERR_INTERNAL_GPU, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return m;
+}
+
 }  // namespace fg

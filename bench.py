@@ -58,6 +58,12 @@ def parse():
                     help="only time the dequant-GEMV on the layer shapes (the profiling case)")
     ap.add_argument("--gemm-table", action="store_true",
                     help="the Q4_0 dequant-GEMV/GEMM table: 4096x11008 and 11008x4096 at batch 1/8/32/128")
+    ap.add_argument("--gemm-case", default="",
+                    help="profiling case M,N,K: `warmup` + `steps` launches of one Q4_0 GEMM (x [M,K] fp32, "
+                         "W [N,K]); prints its event-timed launch time")
+    ap.add_argument("--attention-case", default="",
+                    help="flash-attention prefill B,H,S,d (causal, fp16 Q/K/V ~ N(0,1), scale 1/sqrt(d)): "
+                         "`warmup` + `steps` calls; prints TFLOP/s and the tensor-core fraction")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="profiling case: a model of this many 7B layers at context 4096, `steps` decode steps; "
                          "prints no bench line")
@@ -274,6 +280,58 @@ def gemm_table(ctx, reps=8, rounds=10):
     return rows
 
 
+def gemm_case(ctx, spec, warmup, steps):
+    """One Q4_0 GEMM shape, launched warmup + steps times on the library stream
+    (for ncu captures: the first `warmup` launches are the ones to skip)."""
+    M, N, K = (int(v) for v in spec.split(","))
+    stream = torch.cuda.ExternalStream(ctx.stream_ptr())
+    w = ctx.synth_quant("Q4_0", N, K, seed=77, std=0.02)
+    x = ctx.synth_normal((M, K), np.float32, seed=K + M)
+    out = ctx.empty((M, N), np.float32)
+    for _ in range(warmup):
+        ctx.qmatmul_into(x, w, out)
+    with torch.cuda.stream(stream):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            ctx.qmatmul_into(x, w, out)
+        e1.record()
+    e1.synchronize()
+    us = 1000 * e0.elapsed_time(e1) / steps
+    for h in (w, x, out):
+        ctx.dispose(h)
+    return {"gemm_case": {"M": M, "N": N, "K": K}, "launches": warmup + steps, "us_per_launch": us,
+            "TFLOPs": 2.0 * M * N * K / us / 1e6, "note": "two kernels per launch: k_x_to_f16, k_qgemm_tc"}
+
+
+def attention_case(ctx, spec, warmup, steps):
+    """Causal flash-attention prefill on seeded fp16 inputs [B, H, S, d], timed
+    with CUDA events on the library stream (FLOPs = 4 B H S^2 d / 2)."""
+    B, H, S, d = (int(v) for v in spec.split(","))
+    stream = torch.cuda.ExternalStream(ctx.stream_ptr())
+    q, k, v = (ctx.synth_normal((B, H, S, d), np.float16, seed=SEED + i) for i in range(3))
+    for _ in range(warmup):
+        ctx.dispose(ctx.flashAttention(q, k, v, isCausal=True))
+    outs = []
+    with torch.cuda.stream(stream):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            outs.append(ctx.flashAttention(q, k, v, isCausal=True))
+        e1.record()
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    for h in outs + [q, k, v]:
+        ctx.dispose(h)
+    flops = 4.0 * B * H * S * S * d / 2
+    with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+        peak_tf = float(json.load(f).get("bf16_tflops", 1590.0))
+    return {"attention_case": {"B": B, "H": H, "S": S, "d": d, "causal": True, "dtype": "fp16 in, fp32 out"},
+            "calls": warmup + steps, "ms_per_call": ms, "TFLOPs": flops / ms / 1e9,
+            "tensor_frac": flops / ms / 1e9 / peak_tf, "peak_TFLOPs": peak_tf,
+            "path": os.environ.get("FORGE_B200_ATTN", "tcgen05")}
+
+
 def ctx_stream(ctx):
     import ctypes
     from forge_b200 import _capi as C
@@ -367,6 +425,16 @@ def main():
         ctx = forge_b200.Context(device=local)
         for r in gemm_table(ctx):
             print(json.dumps(r), flush=True)
+        ctx.shutdown()
+        return
+    if args.attention_case:
+        ctx = forge_b200.Context(device=local)
+        print(json.dumps(attention_case(ctx, args.attention_case, args.warmup, args.steps)), flush=True)
+        ctx.shutdown()
+        return
+    if args.gemm_case:
+        ctx = forge_b200.Context(device=local)
+        print(json.dumps(gemm_case(ctx, args.gemm_case, args.warmup, args.steps)), flush=True)
         ctx.shutdown()
         return
     if args.roofline_only:

@@ -49,6 +49,26 @@ def test_fp16_prefill_vs_oracle(ctx):
     assert max_rel_err(out, ref) <= 2e-3
 
 
+@pytest.mark.parametrize("B,H,Hkv,Nq,Nkv,d,causal", [
+    (1, 2, 2, 128, 128, 128, True),    # one query block, one key block, diagonal mask
+    (1, 4, 1, 200, 333, 64, True),     # GQA 4:1, ragged blocks, KV offset 133
+    (2, 2, 2, 256, 256, 128, False),   # non-causal, two batches
+    (1, 2, 2, 130, 100, 128, True),    # more queries than keys: the first 30 rows see none
+    (1, 8, 2, 16, 700, 128, True),     # a 16-token chunk over a 700-token cache
+    (1, 2, 1, 640, 640, 64, True),     # five query blocks, O rescaled across five key blocks
+])
+def test_fp16_tensor_core_vs_oracle(ctx, B, H, Hkv, Nq, Nkv, d, causal):
+    """fp16 Q/K/V with head_dim 64/128 take the tcgen05 kernel (attention_tc.cu)."""
+    q16 = O.f32_to_f16(O.normal(21, 0, B * H * Nq * d)).reshape(B, H, Nq, d)
+    k16 = O.f32_to_f16(O.normal(22, 0, B * Hkv * Nkv * d)).reshape(B, Hkv, Nkv, d)
+    v16 = O.f32_to_f16(O.normal(23, 0, B * Hkv * Nkv * d)).reshape(B, Hkv, Nkv, d)
+    out = ctx.read(ctx.flashAttention(ctx.upload(q16.view(np.float16)), ctx.upload(k16.view(np.float16)),
+                                      ctx.upload(v16.view(np.float16)), isCausal=causal))
+    ref = O.attention(O.f16_to_f32(q16), O.f16_to_f32(k16), O.f16_to_f32(v16), 1 / np.sqrt(d), causal)
+    assert np.isfinite(out).all()
+    assert max_rel_err(out, ref) <= 2e-3
+
+
 def test_validation_messages(ctx):
     q = ctx.upload(np.zeros((1, 3, 4, 8), np.float32))
     k = ctx.upload(np.zeros((1, 2, 4, 8), np.float32))
