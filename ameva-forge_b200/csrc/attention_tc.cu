@@ -14,16 +14,24 @@
 //    core computes block j + 1's scores while block j is in softmax, and
 //    O += P V (N = head_dim, K = 128 keys, V read MN-major) into a TMEM
 //    accumulator;
-//  * four softmax warps own the TMEM lanes = query rows: they read a row of S
+//  * eight softmax warps own the TMEM lanes = query rows, two warps per
+//    32-lane quadrant, each taking 64 of the block's 128 keys (both read the
+//    whole row for its maximum, so they agree on m without exchanging it):
+//    they read S
 //    (tcgen05.ld), apply the scale and the causal/extent mask, update the
-//    running max m and sum l (exp2 domain), write P as fp16 into a swizzled
-//    shared tile, and rescale the O row in TMEM when m grew;
-//  * the same warps finish with out = O / max(l, 1e-12) in fp32.
+//    running max m and sum l (exp2 domain), and write P as fp16 into one of
+//    two swizzled shared tiles.  m moves only when a row's maximum grows by
+//    more than 2^8 (P then stays <= 256, exact in fp16 range); only then is
+//    the O row rescaled in TMEM, so most blocks need no O round trip and the
+//    softmax of block j overlaps P V of block j - 1;
+//  * the same warps finish with out = O / max(l, 1e-12) in fp32, each warp of
+//    a pair storing half of the head columns.
 // Every wait is bounded (tma.cuh); on a timeout the device error word is set
 // and the CTA skips its stores, drains its copies and frees its TMEM.
 #include <cstdlib>
 #include <string>
 
+#include "q4_gemv.cuh"
 #include "runtime.cuh"
 #include "tcgen05.cuh"
 #include "tmap.cuh"
@@ -33,12 +41,13 @@ namespace {
 
 constexpr int kFaRows = 128;  // queries per CTA: UMMA M, TMEM lanes
 constexpr int kFaKeys = 128;  // keys per block: N of S = Q K^T, K of O += P V
-constexpr int kFaSoftmaxWarps = 4;
-constexpr int kFaMmaWarp = 5;  // warp 4 loads K/V
-constexpr int kFaThreads = 6 * 32;
+constexpr int kFaSoftmaxWarps = 8;
+constexpr int kFaMmaWarp = 9;  // warp 8 loads K/V
+constexpr int kFaThreads = 10 * 32;
 constexpr int kFaTmemCols = 512;  // S0 [0, 128), S1 [128, 256), O [256, 256 + head_dim)
 constexpr int kFaOCol = 256;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLazy = 8.f;  // log2 of the largest P before the reference max moves
 
 template <int D>
 struct FaGeo {
@@ -46,7 +55,8 @@ struct FaGeo {
   static constexpr int AtomBytes = 128 * 128;           // [128 rows][64] fp16
   static constexpr int QBytes = Atoms * AtomBytes;      // Q tile, K-major
   static constexpr int KVBytes = Atoms * AtomBytes;     // one K or V block
-  static constexpr int PBytes = 2 * AtomBytes;          // P tile [2 atoms of 64 keys][128 rows][64]
+  static constexpr int PTile = 2 * AtomBytes;           // P tile [2 atoms of 64 keys][128 rows][64]
+  static constexpr int PBytes = 2 * PTile;              // two P tiles
   static constexpr size_t KOff = QBytes, VOff = KOff + 2 * (size_t)KVBytes, POff = VOff + 2 * (size_t)KVBytes;
   // + 1 KB for the 1024-byte alignment; at least 120 KB, so that one CTA
   // holds an SM (it allocates 512 TMEM columns)
@@ -72,7 +82,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   extern __shared__ __align__(1024) unsigned char fa_smem_raw[];
   unsigned char *sm = fa_smem_raw + ((1024 - (smem_u32(fa_smem_raw) & 1023)) & 1023);
   unsigned char *qs = sm, *ks = sm + G::KOff, *vs = sm + G::VOff, *ps = sm + G::POff;
-  __shared__ __align__(8) uint64_t kfull[2], kempty[2], vfull[2], vempty[2], sfull[2], pfull, pvdone, qready;
+  __shared__ __align__(8) uint64_t kfull[2], kempty[2], vfull[2], vempty[2], sfull[2], pvdone[2], pfull, qready;
   __shared__ uint32_t s_taddr;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -101,9 +111,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       mbar_init(&vfull[s], 1);
       mbar_init(&vempty[s], 1);
       mbar_init(&sfull[s], 1);
+      mbar_init(&pvdone[s], 1);  // P V of the blocks using P tile s
     }
     mbar_init(&pfull, kFaSoftmaxWarps);
-    mbar_init(&pvdone, 1);
     mbar_init(&qready, kFaSoftmaxWarps);
     fence_barrier_init();
   }
@@ -115,12 +125,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   bool ok = true;
 
   if (warp < kFaSoftmaxWarps) {
-    // ================= softmax warps: thread = query row = TMEM lane =================
-    const int r = tid, qi = i0 + r;
-    {  // this row of Q, fp16, into the K-major swizzled tile (row r at r * 128, chunk c at c ^ (r & 7))
+    // ================= softmax warps: thread = query row = TMEM lane, warp half hh of the keys =========
+    const int quad = warp & 3, hh = warp >> 2, r = 32 * quad + lane, qi = i0 + r;
+    {  // this row's half of Q, fp16, into the K-major swizzled tile (row r at r * 128, chunk c at c ^ (r & 7))
       const int64_t qoff = (int64_t)b * a.q_sb + (int64_t)h * a.q_sh + (int64_t)qi * a.q_si;
 #pragma unroll 4
-      for (int c = 0; c < D / 8; ++c) {  // 16-byte chunk c: head columns 8c .. 8c+7
+      for (int c = hh * (D / 16); c < (hh + 1) * (D / 16); ++c) {  // 16-byte chunk c: head columns 8c .. 8c+7
         uint4 v = make_uint4(0u, 0u, 0u, 0u);
         if (qi < a.Nq) {
           if (a.q_f16) {
@@ -141,56 +151,89 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 
     const float sl2 = a.scale * kLog2e;  // scores in log2 units
     const int lim = a.causal ? min(nkv - a.Nq + qi + 1, nkv) : nkv;  // keys [0, lim) visible to this row
-    float m = -1e30f * kLog2e, l = 0.f;
-    const uint32_t trow = taddr + ((uint32_t)(32 * warp) << 16), to = trow + kFaOCol;
+    float m = -1e30f * kLog2e, l = 0.f;  // l: this warp's half of the row sum
+    const uint32_t trow = taddr + ((uint32_t)(32 * quad) << 16), to = trow + kFaOCol + hh * (D / 2);
     for (int j = 0; j < nblk; ++j) {
-      const int sb = j & 1, k0 = j * kFaKeys;
+      const int sb = j & 1, kh = j * kFaKeys + hh * 64;  // first key of this warp's half
       ok = ok && mbar_wait(&sfull[sb], (uint32_t)(j >> 1) & 1, a.err, DEVERR_ATTN_FULL);
       __syncwarp();
       tc_fence_after();
-      const uint32_t ts = trow + sb * kFaKeys;
-      const bool masked = k0 + kFaKeys > lim;
-      float v[32], mx = -INFINITY;
+      const uint32_t ts = trow + sb * kFaKeys + hh * 64;
+      const bool masked = kh + 64 > lim;
+      const int ko = j * kFaKeys + (hh ^ 1) * 64;  // first key of the partner warp's half
+      // the whole row in one go (own half kept for the exponentials), one wait
+      uint32_t s0[32], s1[32], x0[32], x1[32];
+      tmem_ld32_issue(ts, s0);
+      tmem_ld32_issue(ts + 32, s1);
+      tmem_ld32_issue(ts + (hh ? -64 : 64), x0);
+      tmem_ld32_issue(ts + (hh ? -32 : 96), x1);
+      tmem_ld_wait(s0);
+      tmem_ld_wait(s1);
+      tmem_ld_wait(x0);
+      tmem_ld_wait(x1);
+      float v[64];  // this warp's 64 scores; masked keys read as -inf (ex2(-inf) = 0)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(ts + 32 * c, v);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) mx = fmaxf(mx, (masked && k0 + 32 * c + e >= lim) ? -INFINITY : v[e]);
+      for (int e = 0; e < 32; ++e) {
+        v[e] = __uint_as_float(s0[e]);
+        v[32 + e] = __uint_as_float(s1[e]);
       }
-      const float m_new = fmaxf(m, mx * sl2), alpha = ex2(m - m_new);
-      if (j > 0) {  // P and O are free once the previous block's P V has completed
-        ok = ok && mbar_wait(&pvdone, (uint32_t)(j - 1) & 1, a.err, DEVERR_ATTN_EMPTY);
+      if (masked) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e)
+          if (kh + e >= lim) v[e] = -INFINITY;
+      }
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int e = 0; e < 64; ++e) mx4[e & 3] = fmaxf(mx4[e & 3], v[e]);  // four independent chains
+      const bool xmasked = ko + 64 > lim;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {  // the partner's half: for the maximum only
+        const float y0 = (xmasked && ko + e >= lim) ? -INFINITY : __uint_as_float(x0[e]);
+        const float y1 = (xmasked && ko + 32 + e >= lim) ? -INFINITY : __uint_as_float(x1[e]);
+        mx4[e & 3] = fmaxf(mx4[e & 3], fmaxf(y0, y1));
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      // the reference max moves only when this row's maximum grew by more than kLazy
+      const float mc = fmaxf(m, mx * sl2);
+      const bool grow = mc - m > kLazy;
+      const bool rescale = __any_sync(0xffffffffu, grow && j > 0);  // same rows, same decision in both warps
+      float alpha = 1.f;
+      if (grow) {
+        alpha = ex2(m - mc);
+        m = mc;
+      }
+      const int pb = j & 1;
+      if (j >= 2) {  // P tile pb is free once P V of block j - 2 has completed
+        ok = ok && mbar_wait(&pvdone[pb], (uint32_t)((j >> 1) - 1) & 1, a.err, DEVERR_ATTN_EMPTY);
         __syncwarp();
-        tc_fence_after();
       }
-      float sum = 0.f;
+      float2 sum2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 sl2x2 = make_float2(sl2, sl2), negm = make_float2(-m, -m);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(ts + 32 * c, v);
+      for (int c = 0; c < 2; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float p0 = ex2(fmaf(v[e], sl2, -m_new)), p1 = ex2(fmaf(v[e + 1], sl2, -m_new));
-          if (masked) {
-            if (k0 + 32 * c + e >= lim) p0 = 0.f;
-            if (k0 + 32 * c + e + 1 >= lim) p1 = 0.f;
-          }
-          sum += p0 + p1;
-          pk[e >> 1] = pack_f16x2(p0, p1);
+          const float2 x = ffma2(make_float2(v[32 * c + e], v[32 * c + e + 1]), sl2x2, negm);
+          const float2 p = make_float2(ex2(x.x), ex2(x.y));
+          sum2[(e >> 1) & 1] = fadd2(sum2[(e >> 1) & 1], p);
+          pk[e >> 1] = pack_f16x2(p.x, p.y);
         }
-        // keys 32c .. 32c+31 of the row: atom c / 2, 16-byte chunks 4 (c % 2) .. +3
-        unsigned char *prow = ps + (c >> 1) * G::AtomBytes + r * 128;
+        // keys 64 hh + 32c .. +31 of the row: atom hh, 16-byte chunks 4c .. 4c+3
+        unsigned char *prow = ps + pb * G::PTile + hh * G::AtomBytes + r * 128;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const int cc = (c & 1) * 4 + q;
+          const int cc = 4 * c + q;
           *reinterpret_cast<uint4 *>(prow + ((cc ^ (r & 7)) * 16)) =
               make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
         }
       }
-      // O *= alpha before this block's P V accumulates into it (whole warp: TMEM moves are warp-wide)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      if (rescale) {  // O *= alpha (this warp's half of the columns) once P V of block j - 1 is in
+        ok = ok && mbar_wait(&pvdone[pb ^ 1], (uint32_t)((j - 1) >> 1) & 1, a.err, DEVERR_ATTN_EMPTY);
+        __syncwarp();
+        tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < D / 64; ++c) {
           float o[32];
           tmem_ld32(to + 32 * c, o);
 #pragma unroll
@@ -202,16 +245,20 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&pfull);
-      l = l * alpha + sum;
-      m = m_new;
+      l = l * alpha + ((sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y));
     }
-    ok = ok && mbar_wait(&pvdone, (uint32_t)(nblk - 1) & 1, a.err, DEVERR_ATTN_FULL);
+    ok = ok && mbar_wait(&pvdone[(nblk - 1) & 1], (uint32_t)((nblk - 1) >> 1) & 1, a.err, DEVERR_ATTN_FULL);
     __syncwarp();
     tc_fence_after();
+    // row sum = the two halves; the Q tile is free once the last MMA has completed
+    float *xsum = reinterpret_cast<float *>(qs);
+    xsum[hh * kFaRows + r] = l;
+    named_sync_id(1 + quad, 64);
+    l += xsum[(hh ^ 1) * kFaRows + r];
     const float inv = 1.f / fmaxf(l, 1e-12f);
-    float *orow = a.o + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + (int64_t)qi * a.o_si;
+    float *orow = a.o + (int64_t)b * a.o_sb + (int64_t)h * a.o_sh + (int64_t)qi * a.o_si + hh * (D / 2);
 #pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
+    for (int c = 0; c < D / 64; ++c) {
       float o[32];
       tmem_ld32(to + 32 * c, o);
       if (ok && qi < a.Nq) {
@@ -256,20 +303,20 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         if (ok) {
 #pragma unroll
           for (int kk = 0; kk < kFaKeys / 16; ++kk) {  // K = 16 keys per MMA
-            const uint64_t dp = smem_desc_sw128(pa + (kk >> 2) * G::AtomBytes + 32 * (kk & 3));
+            const uint64_t dp = smem_desc_sw128(pa + (j & 1) * G::PTile + (kk >> 2) * G::AtomBytes + 32 * (kk & 3));
             // V block [atom of 64 head columns][128 keys][64], MN-major: 16 keys = 2048 bytes
             // per step, 8-key atoms 1024 bytes apart, the next 64 head columns one atom further
             const uint64_t dv = smem_desc_sw128(va + kk * 2048, G::AtomBytes, 1024);
             umma_f16(taddr + kFaOCol, dp, dv, idO, (j > 0 || kk > 0) ? 1u : 0u);
           }
         }
-        umma_commit(&pvdone);
+        umma_commit(&pvdone[j & 1]);
         umma_commit(&vempty[sb]);
         if (j + 2 < nblk) issue_s(j + 2);  // the softmax has finished reading S[j % 2]
       }
     }
   } else if (lane == 0) {
-    // ================= loader: K and V blocks, two slots each =================
+    // ================= loader (warp 8): K and V blocks, two slots each =================
     const uint64_t pol = l2_evict_last_policy();  // re-read by the other query blocks and GQA heads
     tma_prefetch_desc(&tmk);
     tma_prefetch_desc(&tmv);
