@@ -65,8 +65,9 @@ __device__ __forceinline__ int ld_volatile_int(const int *p) { return *reinterpr
 // reaches (E * barriers_per_launch + k + 1) * CTAs, so an arrival is one
 // posted atomic add and the wait is a bounded acquire poll.
 __device__ bool grid_sync(unsigned long long *count, unsigned long long target, int *err) {
-  __threadfence();
-  atomicAdd(count, 1ull);
+  // release: this CTA's phase results (ordered before this thread by the CTA barrier) are visible
+  // to every CTA that acquires the count
+  asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(count) : "memory");
   if (ld_acquire_u64(count) >= target) return true;
   const uint64_t t0 = global_ns();
   for (;;) {
