@@ -44,12 +44,25 @@ constexpr int kStepThreads = kStepConsumers + kStepGroups * 32;  // + one produc
 constexpr int kKeysPerTile = 32;
 constexpr int kBarConsumers = 3;                                 // named barrier of all consumer warps
 
-enum Phase { PH_EMBED, PH_QKV, PH_ATTN, PH_O, PH_GATEUP, PH_DOWN, PH_LM, PH_ARGMAX };
+enum Phase { PH_EMBED, PH_QKV, PH_ATTN, PH_O, PH_GATEUP, PH_DOWN, PH_LM, PH_ARGMAX, PH_COMB };
 
-__device__ __forceinline__ Phase phase_kind(int p, int L) {
+// Phases of a layer: QKV, ATTN, O, GATEUP, DOWN; under tensor parallelism (per = 7) O and DOWN
+// produce partial sums that every rank exchanges, and a COMB phase after each adds them to h.
+__device__ __forceinline__ Phase phase_kind(int p, int L, int per) {
   if (p == 0) return PH_EMBED;
-  if (p <= 5 * L) return (Phase)(PH_QKV + (p - 1) % 5);
-  return p == 5 * L + 1 ? PH_LM : PH_ARGMAX;
+  if (p <= per * L) {
+    const int k = (p - 1) % per;
+    if (per == 5) return (Phase)(PH_QKV + k);
+    // QKV, ATTN, O, COMB, GATEUP, DOWN, COMB
+    if (k == 3 || k == 6) return PH_COMB;
+    return (Phase)(PH_QKV + (k < 3 ? k : k - 1));
+  }
+  return p == per * L + 1 ? PH_LM : PH_ARGMAX;
+}
+// Exchange index within the launch of an O / DOWN phase (or the COMB after it).
+__device__ __forceinline__ int xchg_index(int p, int per) {
+  const int l = (p - 1) / per, k = (p - 1) % per;
+  return 2 * l + (k >= 4 ? 1 : 0);
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
@@ -58,6 +71,33 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   return v;
 }
 __device__ __forceinline__ int ld_volatile_int(const int *p) { return *reinterpret_cast<const volatile int *>(p); }
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long *p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Flag words of rank r's exchange region (pflag[8], key[8], kflag[8]).
+__device__ __forceinline__ unsigned long long *xflag_words(const StepArgs &A, int r) {
+  return reinterpret_cast<unsigned long long *>(reinterpret_cast<unsigned char *>(A.xr[r]) + A.xflags);
+}
+// Wait until every other rank has published sequence `seq` in this rank's word array w[8] (bounded).
+__device__ __noinline__ bool wait_peers(const StepArgs &A, const unsigned long long *w, unsigned long long seq) {
+  const uint64_t t0 = global_ns();
+  for (int r = 0; r < A.tp; ++r) {
+    if (r == A.rank) continue;
+    while (ld_acquire_sys_u64(w + r) < seq) {
+      if (ld_volatile_int(A.err) != 0) return false;
+      if (global_ns() - t0 > kWaitTimeoutNs) {
+        atomicCAS(A.err, 0, DEVERR_GRID);
+        return false;
+      }
+    }
+  }
+  return true;
+}
 
 // Grid-wide barrier, one calling thread per CTA (after a CTA-wide barrier).
 // bar[0] counts arrivals and is never reset; bar[1] counts launches (the
@@ -97,9 +137,50 @@ __device__ __forceinline__ AttnSplit attn_split(int npos, int Hkv, int P) {
 
 }  // namespace
 
+// COMB phase of one group: h[e0, e1) += the partial sums of every rank for exchange xi, in rank order
+// (the same order on every rank, so h stays bit-identical across ranks).  False on a timeout.
+__device__ __noinline__ bool comb_slice(const StepArgs &A, int xi, unsigned long long seq, int e0, int e1, int gtid,
+                                        int gbar, int *s_flag) {
+  if (gtid == 0) *s_flag = wait_peers(A, xflag_words(A, A.rank), seq) ? 0 : -1;
+  named_sync_id(gbar, kGroupThreads);
+  if (*s_flag != 0) return false;
+  const float *part = A.xr[A.rank] + (int64_t)(xi & 1) * A.tp * A.H;
+  for (int e = e0 + gtid; e < e1; e += kGroupThreads) {
+    float v = A.h[e];
+    for (int r = 0; r < A.tp; ++r) v += __ldcg(part + (int64_t)r * A.H + e);
+    A.h[e] = v;
+  }
+  return true;
+}
+
+// The greedy pick over every rank's vocabulary shard: publish this rank's best key to the others,
+// wait for theirs, return the maximum (or `key` unchanged and false on a timeout).
+__device__ __noinline__ bool exchange_keys(const StepArgs &A, unsigned long long kseq, unsigned long long &key) {
+  for (int r = 0; r < A.tp; ++r) {
+    if (r == A.rank) continue;
+    unsigned long long *wr = xflag_words(A, r);
+    wr[8 + A.rank] = key;
+    st_release_sys_u64(wr + 16 + A.rank, kseq);
+  }
+  const unsigned long long *wl = xflag_words(A, A.rank);
+  if (!wait_peers(A, wl + 16, kseq)) return false;
+  for (int r = 0; r < A.tp; ++r)
+    if (r != A.rank) {
+      const unsigned long long kr = *reinterpret_cast<const volatile unsigned long long *>(wl + 8 + r);
+      key = kr > key ? kr : key;
+    }
+  return true;
+}
+
 // GEMV operand of phase p (layer l).
 __device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, QMat &w, const float *&x,
                                            const float *&gamma, Epilogue &ep) {
+  const auto xchg = [&](Epilogue &e, int xi) {  // partial sums to every rank's part[xi % 2][this rank]
+    e.mode = EPI_XCHG;
+    e.xdst = A.xr;
+    e.xoff = ((int64_t)(xi & 1) * A.tp + A.rank) * A.H;
+    e.nx = A.tp;
+  };
   ep = Epilogue();
   if (ph == PH_LM) {
     w = A.lm_head;
@@ -107,7 +188,7 @@ __device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, Q
     gamma = A.norm;
     ep.mode = EPI_PLAIN;
     ep.y = A.logits;
-    ep.ldy = A.vocab;
+    ep.ldy = A.vocab_l;
     return;
   }
   const StepLayer &Ly = A.layers[l];
@@ -136,6 +217,7 @@ __device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, Q
       ep.y = A.h;
       ep.resid = A.h;
       ep.ldy = A.H;
+      if (A.tp > 1) xchg(ep, 2 * l);
       break;
     case PH_GATEUP:
       w = Ly.gateup;
@@ -153,6 +235,7 @@ __device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, Q
       ep.y = A.h;
       ep.resid = A.h;
       ep.ldy = A.H;
+      if (A.tp > 1) xchg(ep, 2 * l + 1);
       break;
   }
 }
@@ -326,7 +409,9 @@ __device__ __forceinline__ void attn_step(const __half *kt0, const __half *kt1, 
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int D, int G>
+// TP: the tensor-parallel instance (O / DOWN partial sums exchanged over NVLink, COMB phases, the
+// greedy pick across vocabulary shards); the single-GPU instance carries none of that code.
+template <int D, int G, bool TP>
 __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_constant__ StepArgs A) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   unsigned char *base = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
@@ -338,13 +423,16 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   __shared__ unsigned long long s_key[kStepConsumers / 32];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int L = A.L, nphase = 5 * L + 3;
+  constexpr int per = TP ? 7 : 5;
+  const int L = A.L, nphase = per * L + 3;
   const int P = kStepGroups * gridDim.x;
   unsigned char *rings = base;                                            // [2][stages][18 KB]
   unsigned char *xarea = base + kStepGroups * kStepStages * kQ4TileBytes;  // staged x / attention scratch
   float *reds = reinterpret_cast<float *>(xarea + A.xarea_bytes);         // [2][128]
   const int npos = A.pos[0];                                              // keys already in the cache
   const unsigned long long epoch = *reinterpret_cast<volatile unsigned long long *>(A.bar + 1);
+  // exchange sequence base of this launch (2 L exchanges per launch; tensor parallelism only)
+  const unsigned long long xbase = TP ? *reinterpret_cast<volatile unsigned long long *>(A.xep) : 0ull;
 
   if (tid == 0) {
     for (int g = 0; g < kStepGroups; ++g)
@@ -368,8 +456,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
     int i = 0;
     bool ok = true;
     for (int p = 0; p < nphase && ok; ++p) {
-      const Phase ph = phase_kind(p, L);
-      const int l = (p - 1) / 5;
+      const Phase ph = phase_kind(p, L, per);
+      const int l = (p - 1) / per;
       if (ph == PH_ATTN) {
         const AttnSplit sp = attn_split(npos, A.Hkv, P);
         if (vk >= sp.units) continue;
@@ -412,8 +500,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   int i = 0;  // ring stages consumed
 
   for (int p = 0; p < nphase; ++p) {
-    const Phase ph = phase_kind(p, L);
-    const int l = (p - 1) / 5;
+    const Phase ph = phase_kind(p, L, per);
+    const int l = (p - 1) / per;
     bool ok = true;
     if (ph == PH_EMBED) {
       const int id = A.ids[0];
@@ -523,19 +611,26 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
           }
         }
       }
+    } else if (TP && ph == PH_COMB) {
+      // h += the partial sums of every rank, in rank order (the same order on every rank, so h stays
+      // bit-identical across ranks); each group owns a slice of h
+      const int xi = xchg_index(p, per);
+      const int e0 = (int)((int64_t)vk * A.H / P), e1 = (int)((int64_t)(vk + 1) * A.H / P);
+      if (e1 > e0) ok = comb_slice(A, xi, xbase * (2 * L) + xi + 1, e0, e1, gtid, gbar, &s_last[grp]);
     } else if (ph == PH_ARGMAX) {
-      // slice of the logits -> one key per CTA -> atomicMax
+      // slice of the logits -> one key per CTA -> atomicMax (global vocabulary index)
       unsigned long long best = 0;
-      const int V = A.vocab;
+      const int V = A.vocab_l;
       for (int j = blockIdx.x * kStepConsumers + tid; j < V; j += gridDim.x * kStepConsumers) {
         const float v = __ldcg(A.logits + j);
+        const int jg = j + A.vbase;
         unsigned long long key;
         if (v != v) {
-          key = j == 0 ? ~0ull : 0ull;  // a NaN never wins, except at index 0 (the sampler keeps index 0)
+          key = jg == 0 ? ~0ull : 0ull;  // a NaN never wins, except at index 0 (the sampler keeps index 0)
         } else {
           uint32_t bits = __float_as_uint(v);
           bits = (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
-          key = ((unsigned long long)bits << 32) | (0xFFFFFFFFull - (unsigned long long)j);
+          key = ((unsigned long long)bits << 32) | (0xFFFFFFFFull - (unsigned long long)jg);
         }
         best = key > best ? key : best;
       }
@@ -578,22 +673,36 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
         }
         q4_group_red<1>(red, acc, gw, lane);
         named_sync_id(gbar, kGroupThreads);
-        if (ok) finish_strip<1>(w, ep, u, red, &s_inv, gtid, kGroupThreads);
+        if (ok) finish_strip<1, TP>(w, ep, u, red, &s_inv, gtid, kGroupThreads);
         named_sync_id(gbar, kGroupThreads);
       }
     }
     // ---------------- end of phase: grid barrier
     if (!ok) s_abort = 1;
     named_sync_id(kBarConsumers, kStepConsumers);
+    const bool xphase = TP && (ph == PH_O || ph == PH_DOWN);
+    // the partial sums this CTA stored into peer memory are visible system-wide before the arrival
+    if (tid == 0 && xphase) __threadfence_system();
     if (tid == 0 && !s_abort &&
         !grid_sync(A.bar, (epoch * (unsigned long long)nphase + p + 1) * gridDim.x, A.err))
       s_abort = 1;
+    if (tid == 0 && blockIdx.x == 0 && xphase && !s_abort) {
+      // every CTA of this rank has arrived: publish exchange xi to the other ranks
+      const unsigned long long seq = xbase * (2 * L) + xchg_index(p, per) + 1;
+      __threadfence_system();
+      for (int r = 0; r < A.tp; ++r)
+        if (r != A.rank) st_release_sys_u64(xflag_words(A, r) + A.rank, seq);
+    }
     named_sync_id(kBarConsumers, kStepConsumers);
     if (s_abort) return;
   }
   // ---------------- the token: CTA 0, after the ARGMAX barrier
   if (blockIdx.x == 0 && tid == 0) {
-    const unsigned long long key = *reinterpret_cast<volatile unsigned long long *>(A.argkey);
+    unsigned long long key = *reinterpret_cast<volatile unsigned long long *>(A.argkey);
+    if constexpr (TP) {  // the greedy pick over every rank's vocabulary shard
+      if (!exchange_keys(A, xbase + 1, key)) return;
+      *A.xep = xbase + 1;
+    }
     const int32_t id = (int32_t)(0xFFFFFFFFull - (key & 0xFFFFFFFFull));
     A.ids[0] = id;
     const int st = *A.step;
@@ -614,23 +723,23 @@ size_t step_attn_floats() {
   return (size_t)kStepGroups * AttnCfg<D, G>::SM_END + (size_t)kStepGroups * D;  // + one-key tiles (2 D halves)
 }
 template <int D, int G>
-const void *step_kernel() {
-  return (const void *)k_decode_step<D, G>;
+const void *step_kernel(bool tp) {
+  return tp ? (const void *)k_decode_step<D, G, true> : (const void *)k_decode_step<D, G, false>;
 }
-const void *pick_kernel(int D, int G) {
+const void *pick_kernel(int D, int G, bool tp) {
   if (D == 128) {
     switch (G) {
-      case 1: return step_kernel<128, 1>();
-      case 2: return step_kernel<128, 2>();
-      case 4: return step_kernel<128, 4>();
-      case 8: return step_kernel<128, 8>();
+      case 1: return step_kernel<128, 1>(tp);
+      case 2: return step_kernel<128, 2>(tp);
+      case 4: return step_kernel<128, 4>(tp);
+      case 8: return step_kernel<128, 8>(tp);
     }
   } else if (D == 64) {
     switch (G) {
-      case 1: return step_kernel<64, 1>();
-      case 2: return step_kernel<64, 2>();
-      case 4: return step_kernel<64, 4>();
-      case 8: return step_kernel<64, 8>();
+      case 1: return step_kernel<64, 1>(tp);
+      case 2: return step_kernel<64, 2>(tp);
+      case 4: return step_kernel<64, 4>(tp);
+      case 8: return step_kernel<64, 8>(tp);
     }
   }
   return nullptr;
@@ -654,7 +763,7 @@ size_t attn_floats(int D, int G) {
 }  // namespace
 
 bool decode_step_supported(int d, int G, int qtype, int64_t H, int64_t I, int64_t qdim) {
-  if (qtype != FG_Q4_0 || !pick_kernel(d, G)) return false;
+  if (qtype != FG_Q4_0 || !pick_kernel(d, G, false)) return false;
   const size_t smem = decode_step_smem(d, G, H, I, qdim);
   return smem <= 220 * 1024;  // 227 KB per block, less the kernel's static shared memory
 }
@@ -675,7 +784,7 @@ size_t decode_step_smem(int d, int G, int64_t H, int64_t I, int64_t qdim) {
 int decode_step_vctas(int num_sms) { return kStepGroups * num_sms; }
 
 void launch_decode_step(const StepArgs &A, int num_sms, cudaStream_t s) {
-  const void *kern = pick_kernel(A.d, A.Hq / A.Hkv);
+  const void *kern = pick_kernel(A.d, A.Hq / A.Hkv, A.tp > 1);
   FG_REQUIRE(kern, FG_ERR_SHAPE, "decode step: head_dim %d / GQA group %d unsupported", A.d, A.Hq / A.Hkv);
   const size_t smem = decode_step_smem(A.d, A.Hq / A.Hkv, A.H, A.I, (int64_t)A.Hq * A.d);
   FG_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -19,6 +19,20 @@ __device__ inline void rope_pair(float v0, float v1, float inv_freq, int pos, fl
 __device__ inline float swiglu1(float g, float u) { return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u); }
 
 // Store a finished pair of columns (n even, n+1) for token m.
+// XCHG (tensor-parallel o_proj / down_proj partial sums): the value of column n to every rank's
+// slot, a peer store over NVLink for the other ranks.  Only kernels instantiated for tensor
+// parallelism reach it (finish_strip<MV, true>).
+__device__ inline void epi_xchg_one(const Epilogue &ep, int64_t n, int m, float v) {
+  for (int r = 0; r < ep.nx; ++r) ep.xdst[r][ep.xoff + (int64_t)m * ep.ldy + n] = v;
+}
+__device__ inline void epi_xchg_pair(const Epilogue &ep, int64_t n, int m, float v0, float v1) {
+  for (int r = 0; r < ep.nx; ++r) {
+    float *y = ep.xdst[r] + ep.xoff + (int64_t)m * ep.ldy + n;
+    y[0] = v0;
+    y[1] = v1;
+  }
+}
+
 __device__ inline void epi_store_pair(const Epilogue &ep, int64_t n, int m, float v0, float v1) {
   if (ep.mode == EPI_PLAIN) {
     float *y = ep.y + (int64_t)m * ep.ldy + n;

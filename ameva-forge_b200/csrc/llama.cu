@@ -72,6 +72,9 @@ struct fg_llama {
   std::map<int, cudaGraphExec_t> graphs;
   bool use_step = false;  // batch-1 decode runs the persistent step kernel
   StepArgs step_args{};
+  // tensor-parallel exchange region of this rank (cudaMalloc, shared by IPC) and the peers' mappings
+  void *xbuf = nullptr;
+  void *xpeer[8] = {};
 
   void *dalloc(uint64_t bytes) {
     void *p = ctx->alloc(bytes);
@@ -232,6 +235,60 @@ void read_logits(fg_llama *m, int B, float *host) {
 
 int set_err(int st, const char *msg);
 
+// Tensor-parallel exchange of the persistent decode step: every rank allocates
+// part[2][tp][H] floats + flag words, shares the allocation with the other
+// ranks by CUDA IPC (handles all-gathered over the NCCL communicator), and maps
+// the peers' regions, so the step kernel stores its o_proj / down_proj partial
+// sums straight into every rank's memory over NVLink.
+void setup_exchange(fg_llama *m) {
+  Ctx &c = *m->ctx;
+  const int tp = m->tp;
+  FG_REQUIRE(tp <= 8, FG_ERR_VALIDATION, "tensor parallel degree %d > 8", tp);
+  const uint64_t part = align_up((uint64_t)2 * tp * m->H * 4, 256);
+  const uint64_t bytes = part + 256;  // pflag[8], key[8], kflag[8]
+  FG_CUDA(cudaMalloc(&m->xbuf, bytes));
+  FG_CUDA(cudaMemset(m->xbuf, 0, bytes));
+  cudaIpcMemHandle_t mine;
+  FG_CUDA(cudaIpcGetMemHandle(&mine, m->xbuf));
+  unsigned char *dh = (unsigned char *)m->dalloc((uint64_t)tp * sizeof(mine));
+  c.h2d(dh + (size_t)m->rank * sizeof(mine), &mine, sizeof(mine));
+  ncclResult_t r = nccl().AllGather(dh + (size_t)m->rank * sizeof(mine), dh, sizeof(mine), ncclUint8,
+                                    (ncclComm_t)c.nccl, c.stream);
+  FG_REQUIRE(r == ncclSuccess, FG_ERR_DEVICE, "ncclAllGather(exchange handles): %s", nccl().GetErrorString(r));
+  std::vector<cudaIpcMemHandle_t> all(tp);
+  c.d2h(all.data(), dh, (uint64_t)tp * sizeof(mine));
+  StepArgs &A = m->step_args;
+  for (int k = 0; k < tp; ++k) {
+    if (k == m->rank) {
+      A.xr[k] = (float *)m->xbuf;
+    } else {
+      FG_CUDA(cudaIpcOpenMemHandle(&m->xpeer[k], all[k], cudaIpcMemLazyEnablePeerAccess));
+      A.xr[k] = (float *)m->xpeer[k];
+    }
+  }
+  A.xflags = (int64_t)part;
+  A.xep = (unsigned long long *)m->dalloc(8);
+  FG_CUDA(cudaMemsetAsync(A.xep, 0, 8, c.stream));
+  // every rank has zeroed and mapped its region before any rank's step kernel writes into it
+  float *one = (float *)m->dalloc(4);
+  FG_CUDA(cudaMemsetAsync(one, 0, 4, c.stream));
+  r = nccl().AllReduce(one, one, 1, ncclFloat32, ncclSum, (ncclComm_t)c.nccl, c.stream);
+  FG_REQUIRE(r == ncclSuccess, FG_ERR_DEVICE, "ncclAllReduce(exchange barrier): %s", nccl().GetErrorString(r));
+  c.sync();
+}
+
+void release_exchange(fg_llama *m) {
+  for (int k = 0; k < 8; ++k)
+    if (m->xpeer[k]) {
+      cudaIpcCloseMemHandle(m->xpeer[k]);
+      m->xpeer[k] = nullptr;
+    }
+  if (m->xbuf) {
+    cudaFree(m->xbuf);
+    m->xbuf = nullptr;
+  }
+}
+
 // State of the persistent decode-step kernel (decode_step.cu).
 void setup_step(fg_llama *m) {
   Ctx &c = *m->ctx;
@@ -282,6 +339,11 @@ void setup_step(fg_llama *m) {
   A.gs = c.gemv;
   A.err = c.gemv.err;
   A.xarea_bytes = decode_step_xarea(d, G, m->H, m->I_l, (int64_t)m->Hq_l * d);
+  A.vocab_l = m->V_l;
+  A.vbase = m->rank * m->V_l;
+  A.tp = m->tp;
+  A.rank = m->rank;
+  if (m->tp > 1) setup_exchange(m);
   m->use_step = true;
 }
 
@@ -431,10 +493,12 @@ int fg_llama_create(fg_ctx *ctx_h, const fg_llama_config *cfg, fg_llama **out) {
     // Batch-1 decode runs as one persistent kernel per token where it applies
     // (FORGE_B200_DECODE=layered keeps the per-layer kernels, for comparison).
     const char *mode = std::getenv("FORGE_B200_DECODE");
-    if (tp == 1 && !(mode && std::string(mode) == "layered") &&
+    if (!(mode && std::string(mode) == "layered") &&
         decode_step_supported(d, m->Hq_l / m->Hkv_l, qt, H, m->I_l, (int64_t)m->Hq_l * d))
       setup_step(m.get());
   } catch (...) {
+    c.sync();
+    release_exchange(m.get());
     for (auto &p : m->allocs) c.free_async(p.first, p.second);
     throw;
   }
@@ -449,6 +513,8 @@ int fg_llama_destroy(fg_llama *m) {
     LGuard g(m);
     for (auto &kv : m->graphs) cudaGraphExecDestroy(kv.second);
     m->graphs.clear();
+    m->ctx->sync();
+    release_exchange(m);
     for (auto &p : m->allocs) m->ctx->free_async(p.first, p.second);
     m->ctx->sync();
   }

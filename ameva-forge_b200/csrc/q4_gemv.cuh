@@ -353,8 +353,8 @@ __device__ __forceinline__ void q4_group_red(float *red, float2 (&acc)[Q4X<MV>::
 
 // Finish strip `strip` (rows 16 strip ..): sum the 8 warps' partials of
 // red[8][16][MV] in warp order, scale by mul[m], run the epilogue.  Threads
-// [0, nth) of the group take part.
-template <int MV>
+// [0, nth) of the group take part.  XCHG: the kernel may pass an EPI_XCHG epilogue.
+template <int MV, bool XCHG = false>
 __device__ __forceinline__ void finish_strip(const QMat &w, const Epilogue &ep, int strip, const float *red,
                                              const float *mul, int tid, int nth) {
   for (int q = tid; q < (kQ4StripRows / 2) * MV; q += nth) {
@@ -368,6 +368,15 @@ __device__ __forceinline__ void finish_strip(const QMat &w, const Epilogue &ep, 
     v0 *= mul[m];
     v1 *= mul[m];
     const int64_t n = (int64_t)strip * kQ4StripRows + 2 * p;
+    if constexpr (XCHG) {
+      if (ep.mode == EPI_XCHG) {
+        if (n + 1 < w.N)
+          epi_xchg_pair(ep, n, m, v0, v1);
+        else if (n < w.N)
+          epi_xchg_one(ep, n, m, v0);
+        continue;
+      }
+    }
     if (n + 1 < w.N)
       epi_store_pair(ep, n, m, v0, v1);
     else if (n < w.N && ep.mode == EPI_PLAIN)

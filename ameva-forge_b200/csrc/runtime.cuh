@@ -99,7 +99,7 @@ void launch_synth_quant(int qtype, int64_t N, int64_t K, uint64_t seed, int64_t 
 
 // Fused epilogues shared by the GEMV and GEMM kernels.  Row n of the weight
 // produces column n of y for token m.
-enum EpiMode { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_QKV = 2 };
+enum EpiMode { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_QKV = 2, EPI_XCHG = 3 };
 struct Epilogue {
   int mode = EPI_PLAIN;
   float *y = nullptr;            // PLAIN: [M][ldy]; SWIGLU: [M][ldy] (N/2 columns used)
@@ -113,6 +113,10 @@ struct Epilogue {
   int tokens_per_seq = 1;        // token m belongs to sequence m / tokens_per_seq
   const int *pos = nullptr;      // [B] cache length before this forward
   const float *inv_freq = nullptr;  // [head_dim/2]
+  // XCHG (tensor-parallel partial sums): column n goes to xdst[r] + xoff + n for every rank r < nx
+  float *const *xdst = nullptr;
+  int64_t xoff = 0;
+  int nx = 0;
 };
 
 // gemv.cu: y = x W^T for up to 4 rows of x (the batch-1 decode path).
@@ -194,6 +198,14 @@ struct StepArgs {
   unsigned long long *bar;     // [2] grid barrier: arrivals, launches (never reset)
   int *err;
   uint64_t xarea_bytes;
+  // tensor parallelism (tp > 1): rank r's exchange region at xr[r] (a peer mapping for r != rank):
+  // float part[2][tp][H] (partial sums of o_proj / down_proj by source rank, by exchange parity),
+  // then at byte xflags: u64 pflag[8] (exchange sequence per source), u64 key[8], u64 kflag[8].
+  int tp = 1, rank = 0;
+  float *xr[8] = {};
+  int64_t xflags = 0;
+  unsigned long long *xep = nullptr;  // exchange epoch of this rank (launches; never reset)
+  int vocab_l = 0, vbase = 0;         // logits of this rank: vocab_l rows from global index vbase
 };
 bool decode_step_supported(int d, int G, int qtype, int64_t H, int64_t I, int64_t qdim);
 size_t decode_step_xarea(int d, int G, int64_t H, int64_t I, int64_t qdim);
