@@ -712,6 +712,13 @@ int fg_llama_generate_device(fg_llama *m, int32_t batch, int32_t steps) {
   FG_LAPI_END
 }
 
+int fg_llama_get_config(fg_llama *m, fg_llama_config *cfg) {
+  FG_LAPI_BEGIN
+  FG_REQUIRE(m && cfg, FG_ERR_VALIDATION, "fg_llama_get_config: null argument");
+  *cfg = m->cfg;
+  FG_LAPI_END
+}
+
 int fg_llama_tokens(fg_llama *m, int32_t *host, int64_t count) {
   FG_LAPI_BEGIN
   LGuard g(m);

@@ -7,7 +7,8 @@ ABI is include/forge_b200.h.
 from . import errors
 from ._capi import LIB_PATH, lib
 from .gpu_core import Context, default, device_count, init, nccl_unique_id
+from .gguf import GGUFFile
 from .llama import LLAMA2_7B, TINYLLAMA_1_1B, LlamaConfig, LlamaForCausalLM
 
 __all__ = ["errors", "LIB_PATH", "lib", "Context", "default", "device_count", "init", "nccl_unique_id",
-           "LlamaConfig", "LlamaForCausalLM", "LLAMA2_7B", "TINYLLAMA_1_1B"]
+           "GGUFFile", "LlamaConfig", "LlamaForCausalLM", "LLAMA2_7B", "TINYLLAMA_1_1B"]

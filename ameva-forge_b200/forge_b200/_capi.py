@@ -93,6 +93,15 @@ _SIGS = {
     "fg_llama_decode": [c_vp, c_vp, c_i32, c_vp, c_vp],
     "fg_llama_generate_device": [c_vp, c_i32, c_i32],
     "fg_llama_tokens": [c_vp, c_vp, c_i64],
+    "fg_llama_get_config": [c_vp, P(LlamaConfigC)],
+    "fg_gguf_open": [ctypes.c_char_p, P(c_vp)],
+    "fg_gguf_close": [c_vp],
+    "fg_gguf_tensor_count": [c_vp, P(c_i64)],
+    "fg_gguf_tensor_info": [c_vp, c_i64, P(ctypes.c_char_p), P(c_i32), P(c_i32), P(c_i64), P(c_vp), P(ctypes.c_uint64)],
+    "fg_gguf_meta_number": [c_vp, ctypes.c_char_p, P(ctypes.c_double)],
+    "fg_gguf_meta_string": [c_vp, ctypes.c_char_p, P(ctypes.c_char_p)],
+    "fg_gguf_llama_config": [c_vp, c_i32, c_i32, P(LlamaConfigC)],
+    "fg_llama_load_gguf": [c_vp, c_vp],
 }
 _RESTYPE = {"fg_version": ctypes.c_char_p, "fg_last_error": ctypes.c_char_p, "fg_status_name": ctypes.c_char_p}
 

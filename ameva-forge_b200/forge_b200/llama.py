@@ -77,6 +77,16 @@ class LlamaForCausalLM:
         """Seeded random-init weights (N(0, std) quantized Linears)."""
         C.call("fg_llama_synthesize", self._p, seed & (2**64 - 1), std)
 
+    @classmethod
+    def from_gguf(cls, path: str, ctx: Context | None = None, max_position_embeddings: int = 0, max_batch: int = 1):
+        """A model with the configuration and weights of a llama.cpp-named
+        GGUF file (Q4_0/Q8_0 Linears; each tensor-parallel rank keeps its shard)."""
+        from .gguf import GGUFFile
+        with GGUFFile(path) as g:
+            m = cls(g.llama_config(max_position_embeddings, max_batch), ctx)
+            C.call("fg_llama_load_gguf", m._p, g._p)
+        return m
+
     def load(self, name: str, data: np.ndarray, layer: int = -1):
         """One weight of the full model: GGUF blocks for Linears, fp16 [V, H]
         embedding, fp32 norm gains.  Each TP rank keeps its shard."""

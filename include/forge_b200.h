@@ -263,6 +263,33 @@ int fg_llama_generate_device(fg_llama *m, int32_t batch, int32_t steps);
 /* Copies the ids produced by the last fg_llama_generate_device call,
  * [steps, batch] row-major. */
 int fg_llama_tokens(fg_llama *m, int32_t *host, int64_t count);
+/* The configuration the model was created with. */
+int fg_llama_get_config(fg_llama *m, fg_llama_config *cfg);
+
+/* ---- GGUF files (new: the loader the reference plans, ranked first among
+ * the components after the hot path) -----------------------------------------
+ * GGUF v2/v3 container, memory-mapped and validated on open (lengths and
+ * offsets against the file size; a malformed file gives FG_ERR_VALIDATION).
+ * Tensor dims follow ggml (dims[0] innermost: a Linear [out, in] is
+ * {in, out}); dtype is FG_F32 / FG_F16 / FG_Q4_0 / FG_Q8_0, or -1 for ggml
+ * types this build does not read (their data pointer is null). */
+typedef struct fg_gguf fg_gguf;
+int fg_gguf_open(const char *path, fg_gguf **out);
+int fg_gguf_close(fg_gguf *g);
+int fg_gguf_tensor_count(const fg_gguf *g, int64_t *n);
+int fg_gguf_tensor_info(const fg_gguf *g, int64_t i, const char **name, int32_t *dtype, int32_t *ndim,
+                        int64_t *dims /* [4] */, const void **data, uint64_t *bytes);
+int fg_gguf_meta_number(const fg_gguf *g, const char *key, double *value);
+int fg_gguf_meta_string(const fg_gguf *g, const char *key, const char **value);
+/* LlamaConfig from the llama.* metadata (general.architecture "llama"): vocab
+ * from token_embd.weight, qtype from blk.0.attn_q.weight; max_position <= 0
+ * takes llama.context_length. */
+int fg_gguf_llama_config(const fg_gguf *g, int32_t max_position, int32_t max_batch, fg_llama_config *cfg);
+/* Loads every weight of a llama.cpp-named Llama file into the model (each
+ * rank keeps its shard): token_embd (F16/F32), output_norm, output, and
+ * blk.N.{attn_norm, attn_q, attn_k, attn_v, attn_output, ffn_norm, ffn_gate,
+ * ffn_up, ffn_down}; the Linears must be of the model's qtype. */
+int fg_llama_load_gguf(fg_llama *m, const fg_gguf *g);
 
 #ifdef __cplusplus
 }
