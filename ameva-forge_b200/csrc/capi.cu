@@ -797,6 +797,28 @@ int fg_argmax(fg_ctx *ctx, fg_handle logits, fg_handle *out) {
   FG_API_END
 }
 
+int fg_sample(fg_ctx *ctx, fg_handle logits, double temperature, int32_t top_k, double top_p, int32_t has_seed,
+              uint32_t seed, fg_handle *out) {
+  FG_API_BEGIN
+  Guard g(ctx);
+  Ctx &c = C(ctx);
+  Tensor &lt = c.get(logits);
+  check_f32(lt, "sample");
+  FG_REQUIRE(lt.ndim >= 1 && lt.shape[lt.ndim - 1] > 0, FG_ERR_VALIDATION, "Logits array cannot be empty");
+  const int64_t n = lt.shape[lt.ndim - 1];
+  const int64_t rows = lt.numel() / n;
+  const int64_t shp[1] = {rows};
+  Tensor *o = nullptr;
+  const fg_handle h = c.make(shp, 1, FG_I32, &o);
+  const uint64_t sb = sample_scratch_bytes(rows, n);
+  void *scratch = sb ? c.alloc(sb) : nullptr;
+  launch_sample((const float *)lt.ptr, rows, n, n, temperature, top_k, top_p, has_seed != 0, seed, scratch,
+                (int32_t *)o->ptr, c.stream);
+  if (scratch) c.free_async(scratch, sb);
+  *out = h;
+  FG_API_END
+}
+
 int fg_cast(fg_ctx *ctx, fg_handle x, int32_t dtype, fg_handle *out) {
   FG_API_BEGIN
   Guard g(ctx);

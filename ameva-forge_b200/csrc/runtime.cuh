@@ -223,6 +223,11 @@ void launch_embedding(const void *table, int table_f16, int64_t vocab, int64_t d
                       int64_t n, float *out, cudaStream_t s);
 void launch_add(const float *a, const float *b, int64_t n, float *out, cudaStream_t s);
 void launch_argmax(const float *logits, int64_t rows, int64_t n, int64_t ld, int32_t *out, cudaStream_t s);
+// sample.cu: LLMSampler.sample per row (temperature, top-k, top-p, Xorshift32 seed);
+// scratch of sample_scratch_bytes(rows, V) bytes.
+uint64_t sample_scratch_bytes(int64_t rows, int64_t V);
+void launch_sample(const float *logits, int64_t rows, int64_t V, int64_t ld, double temperature, int top_k,
+                   double top_p, bool has_seed, uint32_t seed, void *scratch, int32_t *out, cudaStream_t s);
 // per-row (value, index) keys for a cross-rank greedy pick: key orders by value
 // then by lower global index; index_base = first global column of this shard.
 void launch_argmax_keys(const float *logits, int64_t rows, int64_t n, int64_t ld, int64_t index_base,

@@ -199,6 +199,11 @@ class Context:
     def argmax(self, logits) -> str:
         return self._op("fg_argmax", _h(logits))
 
+    def sample(self, logits, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0, seed=None) -> str:
+        """LLMSampler.sample (sampling.ts:35-128) per row: I32 [rows]."""
+        return self._op("fg_sample", _h(logits), float(temperature), int(top_k), float(top_p),
+                        0 if seed is None else 1, 0 if seed is None else int(seed) & 0xFFFFFFFF)
+
     def cast(self, x, dtype) -> str:
         return self._op("fg_cast", _h(x), _NP_TO_FG[np.dtype(dtype)])
 

@@ -202,6 +202,14 @@ int fg_add(fg_ctx *ctx, fg_handle a, fg_handle b, fg_handle *out);
 /* Greedy pick per row (LLMSampler.sample, sampling.ts:45-55): I32 [rows]
  * index of the first maximum of each row of logits [rows, n]. */
 int fg_argmax(fg_ctx *ctx, fg_handle logits, fg_handle *out);
+/* LLMSampler.sample (sampling.ts:35-128) on the device, per row of logits
+ * [rows, V] -> I32 [rows]: greedy at temperature <= 1e-5, else top-k (the
+ * reference's partial selection sort for k <= 128, a stable sort otherwise),
+ * softmax at the temperature, top-p cutoff, and a categorical pick with the
+ * first Xorshift32 output of `seed`.  has_seed = 0 draws the seed from the
+ * host's random device (the reference uses Math.random). */
+int fg_sample(fg_ctx *ctx, fg_handle logits, double temperature, int32_t top_k, double top_p, int32_t has_seed,
+              uint32_t seed, fg_handle *out);
 /* Element-type conversion F32 <-> F16 (round to nearest even). */
 int fg_cast(fg_ctx *ctx, fg_handle x, int32_t dtype, fg_handle *out);
 

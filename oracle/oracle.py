@@ -233,6 +233,76 @@ def argmax(logits) -> int:
     return int(lib().fo_argmax(_p(logits, _f32p), logits.size))
 
 
+def xorshift32_first(seed: int) -> float:
+    """The first output of the reference's Xorshift32 generator / 2^32
+    (packages/forge/src/tensor/sampling.ts:20-28: s = (seed >>> 0) || 1)."""
+    x = (int(seed) & 0xFFFFFFFF) or 1
+    x ^= (x << 13) & 0xFFFFFFFF
+    x ^= x >> 17
+    x ^= (x << 5) & 0xFFFFFFFF
+    return x / 4294967296.0
+
+
+def sample(logits, temperature: float = 1.0, top_k: int = 0, top_p: float = 1.0, seed: int = 0) -> int:
+    """LLMSampler.sample with a seed (packages/forge/src/tensor/sampling.ts:35-128),
+    statement by statement: greedy below temperature 1e-5 (:45-55); the
+    partial selection sort with swaps for k <= 128 (:62-76), else a stable
+    descending sort (:78-80); double-precision softmax stored as float32
+    (:82-96); top-p prefix (:98-109); categorical pick on the first
+    Xorshift32 draw (:111-127).  Pure Python: small vocabularies only."""
+    import math
+    lg = np.asarray(logits, dtype=np.float32).reshape(-1)
+    V = lg.size
+    if V == 0:
+        raise ValueError("Logits array cannot be empty")
+    if temperature <= 1e-5:
+        best, bv = 0, lg[0]
+        for i in range(1, V):
+            if lg[i] > bv:
+                bv, best = lg[i], i
+        return best
+    K = top_k if 0 < top_k < V else V
+    idx = list(range(V))
+    if K < V and K <= 128:
+        for i in range(K):
+            mp, mv = i, lg[idx[i]]
+            for j in range(i + 1, V):
+                if lg[idx[j]] > mv:
+                    mv, mp = lg[idx[j]], j
+            idx[i], idx[mp] = idx[mp], idx[i]
+    else:
+        idx.sort(key=lambda a: -float(lg[a]))  # stable, as Array.prototype.sort
+    mx = float(lg[idx[0]]) / temperature
+    cand = np.empty(K, np.float32)
+    tot = 0.0
+    for i in range(K):
+        p = math.exp(float(lg[idx[i]]) / temperature - mx)
+        cand[i] = p
+        tot += p
+    inv = 1.0 / max(tot, 1e-12)
+    for i in range(K):
+        cand[i] = float(cand[i]) * inv
+    cutoff = K
+    if top_p < 1.0:
+        cs = 0.0
+        for i in range(K):
+            cs += float(cand[i])
+            if cs >= top_p:
+                cutoff = i + 1
+                break
+    fs = 0.0
+    for i in range(cutoff):
+        fs += float(cand[i])
+    invf = 1.0 / max(fs, 1e-12)
+    r = xorshift32_first(seed)
+    acc = 0.0
+    for i in range(cutoff):
+        acc += float(cand[i]) * invf
+        if r <= acc:
+            return idx[i]
+    return idx[cutoff - 1]
+
+
 def num_threads() -> int:
     return int(lib().fo_num_threads())
 
