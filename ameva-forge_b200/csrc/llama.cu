@@ -625,6 +625,18 @@ int fg_llama_reset(fg_llama *m) {
   FG_LAPI_END
 }
 
+int fg_llama_set_position(fg_llama *m, int32_t batch, int32_t pos) {
+  FG_LAPI_BEGIN
+  LGuard g(m);
+  FG_REQUIRE(batch >= 1 && batch <= m->max_batch, FG_ERR_SHAPE, "batch %d outside [1, %d]", batch, m->max_batch);
+  FG_REQUIRE(pos >= 0 && pos < m->cap, FG_ERR_SHAPE, "position %d outside [0, %d)", pos, m->cap);
+  std::vector<int32_t> p((size_t)m->max_batch, 0);
+  for (int b = 0; b < batch; ++b) p[(size_t)b] = pos;
+  m->ctx->h2d(m->pos, p.data(), p.size() * 4);
+  m->host_pos = pos;
+  FG_LAPI_END
+}
+
 int fg_llama_position(fg_llama *m, int32_t *pos) {
   FG_LAPI_BEGIN
   *pos = m->host_pos;

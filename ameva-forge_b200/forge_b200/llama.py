@@ -96,6 +96,11 @@ class LlamaForCausalLM:
     def reset(self):
         C.call("fg_llama_reset", self._p)
 
+    def set_position(self, batch: int, pos: int):
+        """Cache length `pos` for sequences [0, batch) without a prefill (the
+        cache keeps its contents: zeros after creation)."""
+        C.call("fg_llama_set_position", self._p, batch, pos)
+
     @property
     def position(self) -> int:
         v = ctypes.c_int32()

@@ -64,6 +64,9 @@ def parse():
     ap.add_argument("--attention-case", default="",
                     help="flash-attention prefill B,H,S,d (causal, fp16 Q/K/V ~ N(0,1), scale 1/sqrt(d)): "
                          "`warmup` + `steps` calls; prints TFLOP/s and the tensor-core fraction")
+    ap.add_argument("--decode-table", action="store_true",
+                    help="decode rows of the scope table: TinyLlama-1.1B shape b1 ctx 2048 (256 tokens), "
+                         "Llama-2-7B shape b1/16/64 ctx 4096; prints one line per row")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="profiling case: a model of this many 7B layers at context 4096, `steps` decode steps; "
                          "prints no bench line")
@@ -236,18 +239,20 @@ def gemv_roofline(ctx, world, reps=8, rounds=10):
 
 
 def gemm_table(ctx, reps=8, rounds=10):
-    """Q4_0 dequant-GEMV/GEMM of the scope table: W [N, K] in {4096 x 11008,
-    11008 x 4096} from N(0, 0.02), x ~ N(0, 1) at batch 1/8/32/128.  Cold L2:
-    every replay rotates over `reps` weight copies (8 x 25.4 MB > 2 x L2).
-    Graph-captured launches on the library stream, CUDA-event timed."""
+    """Dequant-GEMV/GEMM rows of the scope table: Q4_0 W [N, K] in {4096 x
+    11008, 11008 x 4096} at batch 1/8/32/128 and the Q8_0 4096 x 4096 GEMV at
+    batch 1; W from N(0, 0.02), x ~ N(0, 1).  Cold L2: every replay rotates
+    over `reps` weight copies (more than L2 together).  Graph-captured
+    launches on the library stream, CUDA-event timed."""
     stream = torch.cuda.ExternalStream(ctx.stream_ptr())
     peak_bw, _ = measured_peak()
     with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
         peak_tf = float(json.load(f).get("bf16_tflops", 1590.0))
     rows = []
-    for (N, K) in [(4096, 11008), (11008, 4096)]:
-        ws = [ctx.synth_quant("Q4_0", N, K, seed=77 + r, std=0.02) for r in range(reps)]
-        for M in (1, 8, 32, 128):
+    for (qt, N, K, batches) in [("Q4_0", 4096, 11008, (1, 8, 32, 128)), ("Q4_0", 11008, 4096, (1, 8, 32, 128)),
+                                ("Q8_0", 4096, 4096, (1,))]:
+        ws = [ctx.synth_quant(qt, N, K, seed=77 + r, std=0.02) for r in range(reps)]
+        for M in batches:
             x = ctx.synth_normal((M, K), np.float32, seed=K + M)
             out = ctx.empty((M, N), np.float32)
             for w in ws:
@@ -266,9 +271,10 @@ def gemm_table(ctx, reps=8, rounds=10):
                 e1.record()
             e1.synchronize()
             us = 1000 * e0.elapsed_time(e1) / (rounds * reps)
-            byt = N * (K // 32) * 18 + 4 * M * (K + N)
+            byt = N * (K // 32) * (18 if qt == "Q4_0" else 34) + 4 * M * (K + N)
             fl = 2.0 * M * N * K
-            rows.append({"N": N, "K": K, "batch": M, "kernel": "k_qgemv" if M <= 4 else "k_qgemm_tc (tcgen05)",
+            kern = "k_qgemv" if M <= 4 else ("k_qgemm_tc (tcgen05)" if qt == "Q4_0" else "k_qgemm_simt")
+            rows.append({"qtype": qt, "N": N, "K": K, "batch": M, "kernel": kern,
                          "us": us, "GBps": byt / us / 1e3, "TFLOPs": fl / us / 1e6,
                          "hbm_frac": byt / us / 1e3 / peak_bw, "tensor_frac": fl / us / 1e6 / peak_tf})
             del g
@@ -330,6 +336,69 @@ def attention_case(ctx, spec, warmup, steps):
             "calls": warmup + steps, "ms_per_call": ms, "TFLOPs": flops / ms / 1e9,
             "tensor_frac": flops / ms / 1e9 / peak_tf, "peak_TFLOPs": peak_tf,
             "path": os.environ.get("FORGE_B200_ATTN", "tcgen05")}
+
+
+def decode_bytes(shape, batch, pos_mean):
+    """Algorithmic DRAM bytes of one decode step of `batch` sequences at mean
+    cache length pos_mean: every Q4_0 weight once, each sequence's fp16 K/V of
+    keys [0, pos] read once and the new key/value written, norms, embedding
+    rows, and each GEMV's input and output vectors per sequence."""
+    H, I, V, L = shape["hidden_size"], shape["intermediate_size"], shape["vocab_size"], shape["num_hidden_layers"]
+    hq, hkv = shape["num_attention_heads"], shape["num_key_value_heads"]
+    d = H // hq
+    gemvs = [((hq + 2 * hkv) * d, H), (H, hq * d), (2 * I, H), (H, I)]
+    per_layer = sum(q4_bytes(n, k) + 4 * batch * (n + k) for n, k in gemvs) + 2 * H * 4
+    per_layer += batch * (2 * hkv * d * 2 * (pos_mean + 1) + 2 * hkv * d * 2)
+    head = q4_bytes(V, H) + 4 * batch * (V + H) + H * 4 + batch * H * 2
+    return L * per_layer + head
+
+
+def decode_table(local, steps, warmup):
+    """Decode throughput of the scope table's decode rows on one GPU: random-
+    init Q4_0 weights, cache length set to the context without a prefill (the
+    zero-filled cache is read exactly as a filled one), greedy steps timed with
+    CUDA events on the library stream."""
+    import forge_b200
+    from forge_b200.llama import LLAMA2_7B, TINYLLAMA_1_1B
+    peak, _ = measured_peak()
+    rows = []
+    # largest first: the batch-64 cache alone is ~140 GB
+    for name, shape, batch, ctx_len, n_steps in [("llama2-7b", LLAMA2_7B, 64, 4096, steps),
+                                                  ("llama2-7b", LLAMA2_7B, 16, 4096, steps),
+                                                  ("llama2-7b", LLAMA2_7B, 1, 4096, steps),
+                                                  ("tinyllama-1.1b", TINYLLAMA_1_1B, 1, 2048, 256)]:
+        torch.cuda.synchronize(local)
+        free, _ = torch.cuda.mem_get_info(local)
+        ctx = forge_b200.Context(device=local, vram_limit_bytes=int(free * 0.98))
+        stream = torch.cuda.ExternalStream(ctx.stream_ptr())
+        cap = ctx_len + warmup + n_steps + 8
+        m = forge_b200.LlamaForCausalLM(forge_b200.LlamaConfig(max_position_embeddings=cap, max_batch=batch,
+                                                               qtype="Q4_0", **shape), ctx)
+        m.synthesize(SEED)
+        m.set_position(batch, ctx_len)
+        ids = (np.arange(batch, dtype=np.int32) * 7919 + 11) % shape["vocab_size"]
+        m.decode(ids)  # seeds the device-side ids
+        m.generate_device(batch, warmup, read=False)
+        ctx.synchronize()
+        with torch.cuda.stream(stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+        m.generate_device(batch, n_steps, read=False)
+        with torch.cuda.stream(stream):
+            e1.record()
+        ctx.synchronize()
+        ms = e0.elapsed_time(e1)
+        pos_mean = ctx_len + 1 + warmup + (n_steps - 1) / 2.0
+        byt = decode_bytes(shape, batch, pos_mean)
+        sec = ms / 1e3 / n_steps
+        rows.append({"decode": name, "batch": batch, "context": ctx_len, "steps": n_steps,
+                     "tokens_per_s": batch * n_steps / (ms / 1e3), "ms_per_step": ms / n_steps,
+                     "GBps": byt / sec / 1e9, "hbm_frac": byt / sec / 1e9 / peak,
+                     "path": "persistent step kernel" if batch == 1 else "layered kernels (CUDA graph)",
+                     "kv": "cache length set without a prefill (zero-filled keys/values, read in full)"})
+        m.close()
+        ctx.shutdown()
+    return rows
 
 
 def ctx_stream(ctx):
@@ -426,6 +495,10 @@ def main():
         for r in gemm_table(ctx):
             print(json.dumps(r), flush=True)
         ctx.shutdown()
+        return
+    if args.decode_table:
+        for r in decode_table(local, args.steps, args.warmup):
+            print(json.dumps(r), flush=True)
         return
     if args.attention_case:
         ctx = forge_b200.Context(device=local)

@@ -271,6 +271,10 @@ int fg_llama_generate_device(fg_llama *m, int32_t batch, int32_t steps);
 /* Copies the ids produced by the last fg_llama_generate_device call,
  * [steps, batch] row-major. */
 int fg_llama_tokens(fg_llama *m, int32_t *host, int64_t count);
+/* Sets the cache length of sequences [0, batch) to `pos` without running a
+ * prefill: positions [0, pos) keep whatever the cache holds (zeros after
+ * creation).  For decode measurements at a given context. */
+int fg_llama_set_position(fg_llama *m, int32_t batch, int32_t pos);
 /* The configuration the model was created with. */
 int fg_llama_get_config(fg_llama *m, fg_llama_config *cfg);
 
