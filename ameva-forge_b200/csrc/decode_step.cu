@@ -130,7 +130,7 @@ struct AttnSplit {
 __device__ __forceinline__ AttnSplit attn_split(int npos, int Hkv, int P) {
   AttnSplit a;
   a.nt = (npos + kKeysPerTile - 1) / kKeysPerTile;
-  a.S = max(1, min(P / Hkv, a.nt));
+  a.S = max(1, min(min(P / Hkv, 512), a.nt));  // <= 512: the merge weights [S][G] fit the 8 G D o area
   a.units = Hkv * a.S;
   return a;
 }
@@ -244,163 +244,209 @@ namespace {
 
 // ---------------------------------------------------------------------------
 // Attention consumer: one unit (KV head hk, keys of tiles [t0, t1) + the
-// current key when `last`) on the 256 threads of a group.  Tile layout in a
-// ring slot: K rows [32][D] fp16, then V rows [32][D] fp16.
+// current key when `last`) on the 8 warps of a group.  Tile layout in a ring
+// slot: K rows [32][D] fp16, then V rows [32][D] fp16.  Warp w takes keys
+// [4w, 4w + 4) of every tile and keeps its own online softmax (running max,
+// sum and output in registers), so no group barrier runs inside a unit; the
+// eight warp states merge once at its end.
 // ---------------------------------------------------------------------------
 constexpr int r4(int x) { return (x + 3) & ~3; }
 
 template <int D, int G>
 struct AttnCfg {
-  static constexpr int NS = 2;                                 // ring slots (32 keys each) per step
-  static constexpr int KEYS = NS * kKeysPerTile;               // keys per step
-  static constexpr int KW = KEYS / kGroupWarps;                // keys per warp in q.k (lanes: 4 keys x 8 dim chunks)
-  static constexpr int KR = KW / 4;                            // keys per lane in q.k
-  static constexpr int DC = D / 8;                             // dims per lane in q.k
-  static constexpr int PAIRS = D / 2 * G;                      // (g, dim pair) outputs
-  static constexpr int PPT = PAIRS > kGroupThreads ? PAIRS / kGroupThreads : 1;  // pairs per thread
-  static constexpr int KQ = PAIRS >= kGroupThreads ? 1 : kGroupThreads / PAIRS;   // key partitions in p.V
-  static constexpr int KPQ = KEYS / KQ;                        // keys per partition
-  static constexpr int NCH = G * KEYS / 32;                    // 32-entry chunks of p
   static_assert(D == 64 || D == 128, "head_dim");
-  // shared scratch (floats): q [G][D], scores [G][KEYS], p [G][KEYS], warp max [8][G], chunk sums [NCH],
-  // merge [KQ][G][D]
-  static constexpr int SM_Q = 0, SM_S = G * D, SM_P = SM_S + G * KEYS, SM_WM = SM_P + G * KEYS,
-                       SM_PS = SM_WM + 8 * G, SM_O = r4(SM_PS + NCH), SM_END = r4(SM_O + KQ * G * D);
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "GQA group");
+  static constexpr int NV = D / 64;              // q.k: lane 8 kk + c takes 16-byte chunks c + 8 v (v < NV) of key kk
+  static constexpr int DL = D / 32;              // p.V: lane takes dims [DL lane, DL lane + DL)
+  static constexpr int GL = 8 / G;               // lanes of a key that end the score reduction with the same g
+  static constexpr bool QREG = G * NV * 8 <= 32;  // this lane's q slice lives in registers
+  // shared scratch (floats): q [G][D] (chunk halves swizzled), per-warp p [8][G][4] + alpha [8][G],
+  // warp states (m, l) [8][G] and o [8][G][D]; the cross-split merge reuses the o area for its weights
+  static constexpr int SM_Q = 0, SM_P = G * D, SM_ML = r4(SM_P + 8 * G * 5), SM_O = r4(SM_ML + 16 * G),
+                       SM_END = SM_O + 8 * G * D;
 };
 
-template <int D, int G>
-struct AttnState {
-  float m[G], l[G];
-  float2 o[AttnCfg<D, G>::PPT];
-};
+// Offset of q element dd of a row: the two float4 halves of 8-dim chunk k swap places when bit 2 of k is
+// set, so the eight lanes of a key read their chunks' first halves from eight distinct bank groups.
+__device__ __forceinline__ int q_swz(int dd) {
+  const int k = dd >> 3;
+  return (k << 3) | (((dd & 7) + (((k >> 2) & 1) << 2)) & 7);
+}
 
-// One step of up to 64 keys: key j lives in row (j % 32) of slot (j / 32):
-// K rows at kt0 / kt1, V rows at vt0 / vt1 (shared memory); nk keys are valid
-// and rows past nk are never read.
 template <int D, int G>
-__device__ __forceinline__ void attn_step(const __half *kt0, const __half *kt1, const __half *vt0, const __half *vt1,
-                                          int nk, float *sm, AttnState<D, G> &S, int tid, int bar) {
+struct WarpAttn {
   using C = AttnCfg<D, G>;
-  const int lane = tid & 31, warp = tid >> 5;
-  // ---- scores: warp w takes keys [w KW, (w+1) KW); lane (kk, c): keys w KW + 4r + kk, dims [c DC, (c+1) DC)
-  {
-    const int kk = lane >> 3, c = lane & 7;
-    float kf[C::KR][C::DC];
+  float q[C::QREG ? G * C::NV * 8 : 1];  // q[g][chunk c + 8 v][e] of this lane
+  float m, l;                           // running max and sum of this lane's g (= c / GL)
+  float o[G][C::DL];                    // output dims [DL lane, DL lane + DL) of every g
+};
+
+// q element e of chunk (c + 8 v) of row g, read from shared memory (swizzled) or this lane's registers.
+template <int D, int G>
+__device__ __forceinline__ void attn_q8(const WarpAttn<D, G> &W, const float *sq, int g, int v, int c, float (&qv)[8]) {
+  using C = AttnCfg<D, G>;
+  if constexpr (C::QREG) {
 #pragma unroll
-    for (int r = 0; r < C::KR; ++r) {
-      const int j = warp * C::KW + 4 * r + kk;
-      const __half *kr = (j < kKeysPerTile ? kt0 : kt1) + (j % kKeysPerTile) * D + c * C::DC;
+    for (int e = 0; e < 8; ++e) qv[e] = W.q[(g * C::NV + v) * 8 + e];
+  } else {
+    const int k = c + 8 * v, h = (k >> 2) & 1;
+    const float4 a = *reinterpret_cast<const float4 *>(sq + g * D + k * 8 + 4 * h);
+    const float4 b = *reinterpret_cast<const float4 *>(sq + g * D + k * 8 + 4 * (h ^ 1));
+    qv[0] = a.x, qv[1] = a.y, qv[2] = a.z, qv[3] = a.w, qv[4] = b.x, qv[5] = b.y, qv[6] = b.z, qv[7] = b.w;
+  }
+}
+
+template <int D, int G>
+__device__ __forceinline__ void attn_warp_init(WarpAttn<D, G> &W, const float *sq, int lane) {
+  using C = AttnCfg<D, G>;
+  if constexpr (C::QREG) {
+    const int c = lane & 7;
 #pragma unroll
-      for (int v = 0; v < C::DC / 8; ++v) {
-        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-        if (j < nk) raw = *reinterpret_cast<const uint4 *>(kr + 8 * v);
-        const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+    for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __half22float2(h2[e]);
-          kf[r][8 * v + 2 * e] = f.x;
-          kf[r][8 * v + 2 * e + 1] = f.y;
-        }
+      for (int v = 0; v < C::NV; ++v) {
+        const int k = c + 8 * v, h = (k >> 2) & 1;
+        const float4 a = *reinterpret_cast<const float4 *>(sq + g * D + k * 8 + 4 * h);
+        const float4 b = *reinterpret_cast<const float4 *>(sq + g * D + k * 8 + 4 * (h ^ 1));
+        float *d = &W.q[(g * C::NV + v) * 8];
+        d[0] = a.x, d[1] = a.y, d[2] = a.z, d[3] = a.w, d[4] = b.x, d[5] = b.y, d[6] = b.z, d[7] = b.w;
       }
+  }
+  W.m = -INFINITY;
+  W.l = 0.0f;
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int t = 0; t < C::DL; ++t) W.o[g][t] = 0.0f;
+}
+
+// Keys [4w, 4w + 4) of one tile for warp w: key j's K row at kt + j D, its V row at vt + j D; keys
+// j >= nk are masked and their rows never read.  GLB: the rows are in global memory, written by
+// other CTAs of this launch (read through L2).  sp: this warp's p / alpha exchange area (G >= 4).
+template <int D, int G, bool GLB>
+__device__ __forceinline__ void attn_warp_tile(const __half *kt, const __half *vt, int nk, const float *sq, float *sp,
+                                               WarpAttn<D, G> &W, int w, int lane) {
+  using C = AttnCfg<D, G>;
+  const int kk = lane >> 3, c = lane & 7, j = 4 * w + kk;
+  const bool valid = j < nk;
+  // ---- partial dots of this lane's chunks for every g (two chains each)
+  float sa[G], sb[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) sa[g] = sb[g] = 0.0f;
+#pragma unroll
+  for (int v = 0; v < C::NV; ++v) {
+    uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+    if (valid) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(kt + (int64_t)j * D + (c + 8 * v) * 8);
+      raw = GLB ? __ldcg(src) : *src;
+    }
+    float kf[8];
+    const __half2 *h2 = reinterpret_cast<const __half2 *>(&raw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h2[e]);
+      kf[2 * e] = f.x;
+      kf[2 * e + 1] = f.y;
     }
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float *qg = sm + C::SM_Q + g * D + c * C::DC;
-      float sa[C::KR], sb[C::KR];
+      float qv[8];
+      attn_q8<D, G>(W, sq, g, v, c, qv);
 #pragma unroll
-      for (int r = 0; r < C::KR; ++r) sa[r] = sb[r] = 0.0f;
+      for (int e = 0; e < 8; e += 2) {
+        sa[g] = fmaf(qv[e], kf[e], sa[g]);
+        sb[g] = fmaf(qv[e + 1], kf[e + 1], sb[g]);
+      }
+    }
+  }
+  // ---- reduce over the 8 lanes of the key, scattering g: while more than one g is left, each xor round
+  // halves them (the lane with the bit set keeps the upper half); then plain butterfly sums
+  float s[G];
 #pragma unroll
-      for (int e = 0; e < C::DC; e += 4) {
-        const float4 q4 = *reinterpret_cast<const float4 *>(qg + e);
+  for (int g = 0; g < G; ++g) s[g] = sa[g] + sb[g];
+  {
+    int cnt = G;
 #pragma unroll
-        for (int r = 0; r < C::KR; ++r) {
-          sa[r] = fmaf(q4.x, kf[r][e], sa[r]);
-          sb[r] = fmaf(q4.y, kf[r][e + 1], sb[r]);
-          sa[r] = fmaf(q4.z, kf[r][e + 2], sa[r]);
-          sb[r] = fmaf(q4.w, kf[r][e + 3], sb[r]);
+    for (int bit = 4; bit >= 1; bit >>= 1) {
+      if (cnt > 1) {
+        const int h = cnt / 2;
+        const bool up = (c & bit) != 0;
+#pragma unroll
+        for (int i2 = 0; i2 < G / 2; ++i2) {
+          if (i2 < h) {
+            const float send = up ? s[i2] : s[i2 + h];
+            const float keep = up ? s[i2 + h] : s[i2];
+            s[i2] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+          }
         }
+        cnt = h;
+      } else {
+        s[0] += __shfl_xor_sync(0xffffffffu, s[0], bit);
       }
-      float wm = -INFINITY;
+    }
+  }
+  // ---- online softmax of this lane's g over the warp's 4 keys
+  const float sv = valid ? s[0] : -INFINITY;
+  float tm = fmaxf(sv, __shfl_xor_sync(0xffffffffu, sv, 8));
+  tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 16));
+  const float mn = fmaxf(W.m, tm);
+  const float al = mn == -INFINITY ? 1.0f : expf(W.m - mn);
+  const float p = valid ? expf(sv - mn) : 0.0f;
+  float ps = p + __shfl_xor_sync(0xffffffffu, p, 8);
+  ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+  W.l = W.l * al + ps;
+  W.m = mn;
+  // ---- every g's p of the 4 keys and alpha, to every lane
+  float pk[G][4], ag[G];
+  if constexpr (G <= 2) {
 #pragma unroll
-      for (int r = 0; r < C::KR; ++r) {
-        float sv = sa[r] + sb[r];
-        sv += __shfl_xor_sync(0xffffffffu, sv, 1);
-        sv += __shfl_xor_sync(0xffffffffu, sv, 2);
-        sv += __shfl_xor_sync(0xffffffffu, sv, 4);
-        const int j = warp * C::KW + 4 * r + kk;
-        if (j >= nk) sv = -INFINITY;
-        if (c == 0) sm[C::SM_S + g * C::KEYS + j] = sv;
-        wm = fmaxf(wm, sv);
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int k2 = 0; k2 < 4; ++k2) pk[g][k2] = __shfl_sync(0xffffffffu, p, 8 * k2 + g * C::GL);
+      ag[g] = __shfl_sync(0xffffffffu, al, g * C::GL);
+    }
+  } else {
+    __syncwarp();  // the previous tile's reads of sp are done
+    if (c % C::GL == 0) {
+      sp[(c / C::GL) * 4 + kk] = p;
+      if (kk == 0) sp[G * 4 + c / C::GL] = al;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float4 t = *reinterpret_cast<const float4 *>(sp + g * 4);
+      pk[g][0] = t.x, pk[g][1] = t.y, pk[g][2] = t.z, pk[g][3] = t.w;
+      ag[g] = sp[G * 4 + g];
+    }
+  }
+  // ---- o = o alpha + p V over the warp's valid keys
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int t = 0; t < C::DL; ++t) W.o[g][t] *= ag[g];
+#pragma unroll
+  for (int k2 = 0; k2 < 4; ++k2) {
+    const int jj = 4 * w + k2;
+    if (jj < nk) {
+      float vf[C::DL];
+      const __half *vr = vt + (int64_t)jj * D + lane * C::DL;
+      if constexpr (C::DL == 4) {
+        const uint2 *src = reinterpret_cast<const uint2 *>(vr);
+        const uint2 raw = GLB ? __ldcg(src) : *src;
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&raw.y));
+        vf[0] = a.x, vf[1] = a.y, vf[2] = b.x, vf[3] = b.y;
+      } else {
+        const unsigned *src = reinterpret_cast<const unsigned *>(vr);
+        const unsigned raw = GLB ? __ldcg(src) : *src;
+        const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&raw));
+        vf[0] = a.x, vf[1] = a.y;
       }
-      wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 8));
-      wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, 16));
-      if (lane == 0) sm[C::SM_WM + warp * G + g] = wm;
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int t = 0; t < C::DL; ++t) W.o[g][t] = fmaf(pk[g][k2], vf[t], W.o[g][t]);
     }
-  }
-  named_sync_id(bar, kGroupThreads);
-  // ---- new running max; p = exp(s - m') for entries (g, key); sums per 32-entry chunk
-  float mnew[G], alpha[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float tm = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kGroupWarps; ++w) tm = fmaxf(tm, sm[C::SM_WM + w * G + g]);
-    mnew[g] = fmaxf(S.m[g], tm);
-    alpha[g] = mnew[g] == -INFINITY ? 1.0f : expf(S.m[g] - mnew[g]);
-  }
-  for (int idx = tid; idx < G * C::KEYS; idx += kGroupThreads) {
-    const int g = idx / C::KEYS;
-    float mg = -INFINITY;
-#pragma unroll
-    for (int gg = 0; gg < G; ++gg)
-      if (gg == g) mg = mnew[gg];
-    const float sv = sm[C::SM_S + idx];
-    const float p = sv == -INFINITY ? 0.0f : expf(sv - mg);
-    sm[C::SM_P + idx] = p;
-    const float ps = warp_sum(p);  // the warp's 32 entries share g (KEYS is a multiple of 32)
-    if ((idx & 31) == 0) sm[C::SM_PS + (idx >> 5)] = ps;
-  }
-  named_sync_id(bar, kGroupThreads);
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float ps = 0.0f;
-#pragma unroll
-    for (int ch = 0; ch < C::KEYS / 32; ++ch) ps += sm[C::SM_PS + g * (C::KEYS / 32) + ch];
-    S.l[g] = S.l[g] * alpha[g] + ps;
-    S.m[g] = mnew[g];
-  }
-  // ---- o += p V: thread -> (pair slot, key partition kq)
-  const int slot = tid % (C::PAIRS / C::PPT), kq = tid / (C::PAIRS / C::PPT);
-  const int kbeg = kq * C::KPQ, kend = min(kbeg + C::KPQ, nk);
-#pragma unroll
-  for (int r = 0; r < C::PPT; ++r) {
-    const int pr = slot * C::PPT + r;  // (g, dim pair) index
-    const int g = pr / (D / 2), dp = pr % (D / 2);
-    float a = 1.0f;
-#pragma unroll
-    for (int gg = 0; gg < G; ++gg)
-      if (gg == g) a = alpha[gg];
-    const float *pg = sm + C::SM_P + g * C::KEYS;
-    float2 o0 = make_float2(S.o[r].x * a, S.o[r].y * a), o1 = make_float2(0.0f, 0.0f);
-    int j = kbeg;
-    for (; j + 1 < kend; j += 2) {
-      const float2 v0 =
-          __half22float2(reinterpret_cast<const __half2 *>((j < kKeysPerTile ? vt0 : vt1) + (j % kKeysPerTile) * D)[dp]);
-      const float2 v1 = __half22float2(
-          reinterpret_cast<const __half2 *>((j + 1 < kKeysPerTile ? vt0 : vt1) + ((j + 1) % kKeysPerTile) * D)[dp]);
-      const float p0 = pg[j], p1 = pg[j + 1];
-      o0.x = fmaf(p0, v0.x, o0.x);
-      o0.y = fmaf(p0, v0.y, o0.y);
-      o1.x = fmaf(p1, v1.x, o1.x);
-      o1.y = fmaf(p1, v1.y, o1.y);
-    }
-    if (j < kend) {
-      const float2 v0 =
-          __half22float2(reinterpret_cast<const __half2 *>((j < kKeysPerTile ? vt0 : vt1) + (j % kKeysPerTile) * D)[dp]);
-      o0.x = fmaf(pg[j], v0.x, o0.x);
-      o0.y = fmaf(pg[j], v0.y, o0.y);
-    }
-    S.o[r] = make_float2(o0.x + o1.x, o0.y + o1.y);
   }
 }
 
@@ -517,72 +563,65 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
         const int t0 = s * sp.nt / sp.S, t1 = (s + 1) * sp.nt / sp.S;
         const bool last = s == sp.S - 1;
         for (int e = gtid; e < G * D; e += kGroupThreads)
-          sm[Cf::SM_Q + e] = __ldcg(A.q + (int64_t)hk * G * D + e) * A.scale;
-        AttnState<D, G> st;
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          st.m[g] = -INFINITY;
-          st.l[g] = 0.0f;
-        }
-#pragma unroll
-        for (int r = 0; r < Cf::PPT; ++r) st.o[r] = make_float2(0.0f, 0.0f);
+          sm[Cf::SM_Q + (e / D) * D + q_swz(e % D)] = __ldcg(A.q + (int64_t)hk * G * D + e) * A.scale;
         named_sync_id(gbar, kGroupThreads);
-        for (int t = t0; t < t1; t += Cf::NS) {  // two ring slots (64 keys) per step
-          const int ns = min(Cf::NS, t1 - t);
-          const int sl0 = i % kStepStages, sl1 = (i + 1) % kStepStages;
-          ok = ok && mbar_wait(&fl[sl0], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
-          if (ns == 2) ok = ok && mbar_wait(&fl[sl1], (uint32_t)((i + 1) / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
-          const __half *k0 = reinterpret_cast<const __half *>(ring + sl0 * kQ4TileBytes);
-          const __half *k1 = ns == 2 ? reinterpret_cast<const __half *>(ring + sl1 * kQ4TileBytes) : k0;
-          // every thread runs the step (it holds group barriers); without data it takes no keys
-          attn_step<D, G>(k0, k1, k0 + kKeysPerTile * D, k1 + kKeysPerTile * D,
-                          ok ? min(ns * kKeysPerTile, npos - t * kKeysPerTile) : 0, sm, st, gtid, gbar);
+        WarpAttn<D, G> W;
+        attn_warp_init<D, G>(W, sm + Cf::SM_Q, lane);
+        float *wp = sm + Cf::SM_P + gw * G * 5;
+        for (int t = t0; t < t1; ++t, ++i) {
+          const int sl = i % kStepStages;
+          ok = ok && mbar_wait(&fl[sl], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
+          if (ok) {
+            const __half *kt = reinterpret_cast<const __half *>(ring + sl * kQ4TileBytes);
+            attn_warp_tile<D, G, false>(kt, kt + kKeysPerTile * D, min(kKeysPerTile, npos - t * kKeysPerTile),
+                                        sm + Cf::SM_Q, wp, W, gw, lane);
+          }
           __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&em[sl0]);
-            if (ns == 2) mbar_arrive(&em[sl1]);
-          }
-          i += ns;
+          if (lane == 0) mbar_arrive(&em[sl]);
         }
-        if (last) {
-          // key npos (this step's K/V) from global memory into a one-key tile
-          __half *kt = reinterpret_cast<__half *>(reinterpret_cast<float *>(xarea) + kStepGroups * Cf::SM_END) + grp * 2 * D;
-          const __half *kg = A.layers[l].k + ((int64_t)hk * A.cap + npos) * D;
-          const __half *vg = A.layers[l].v + ((int64_t)hk * A.cap + npos) * D;
-          named_sync_id(gbar, kGroupThreads);
-          for (int e = gtid; e < D; e += kGroupThreads) {
-            kt[e] = __ldcg(kg + e);
-            kt[D + e] = __ldcg(vg + e);
-          }
-          named_sync_id(gbar, kGroupThreads);
-          attn_step<D, G>(kt, kt, kt + D, kt + D, ok ? 1 : 0, sm, st, gtid, gbar);
+        if (last && gw == 0 && ok) {  // key npos: this step's K/V, written by the QKV phase of this launch
+          const int64_t row = ((int64_t)hk * A.cap + npos) * D;
+          attn_warp_tile<D, G, true>(A.layers[l].k + row, A.layers[l].v + row, 1, sm + Cf::SM_Q, wp, W, 0, lane);
         }
-        // ---- combine the key partitions, write the unit's partial
-        float *om = sm + Cf::SM_O;  // [KQ][G][D]
+        // ---- merge the eight warp states into the unit's (m, l, o)
+        float *wml = sm + Cf::SM_ML, *wo = sm + Cf::SM_O;
         {
-          const int slot = gtid % (Cf::PAIRS / Cf::PPT), kq = gtid / (Cf::PAIRS / Cf::PPT);
+          const int c = lane & 7;
+          if (lane < 8 && c % Cf::GL == 0) {
+            wml[(gw * G + c / Cf::GL) * 2] = W.m;
+            wml[(gw * G + c / Cf::GL) * 2 + 1] = W.l;
+          }
 #pragma unroll
-          for (int r = 0; r < Cf::PPT; ++r) {
-            const int pr = slot * Cf::PPT + r;
-            const int g = pr / (D / 2), dp = pr % (D / 2);
-            om[(kq * G + g) * D + 2 * dp] = st.o[r].x;
-            om[(kq * G + g) * D + 2 * dp + 1] = st.o[r].y;
+          for (int g = 0; g < G; ++g) {
+            float *dst = wo + (gw * G + g) * D + lane * Cf::DL;
+            if constexpr (Cf::DL == 4)
+              *reinterpret_cast<float4 *>(dst) = make_float4(W.o[g][0], W.o[g][1], W.o[g][2], W.o[g][3]);
+            else
+              *reinterpret_cast<float2 *>(dst) = make_float2(W.o[g][0], W.o[g][1]);
           }
         }
         named_sync_id(gbar, kGroupThreads);
         float *part = A.attn_part + ((int64_t)hk * sp.S + s) * G * (D + 2);
         for (int e = gtid; e < G * D; e += kGroupThreads) {
           const int g = e / D, c = e % D;
-          float o = 0.0f;
+          float M = -INFINITY;
 #pragma unroll
-          for (int kq = 0; kq < Cf::KQ; ++kq) o += om[(kq * G + g) * D + c];
+          for (int w = 0; w < kGroupWarps; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
+          float Ls = 0.0f, O = 0.0f;
+#pragma unroll
+          for (int w = 0; w < kGroupWarps; ++w) {
+            const float mw = wml[(w * G + g) * 2];
+            const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+            Ls = fmaf(wml[(w * G + g) * 2 + 1], f, Ls);
+            O = fmaf(wo[(w * G + g) * D + c], f, O);
+          }
           if (sp.S == 1) {
-            A.att[(int64_t)(hk * G + g) * D + c] = o / fmaxf(st.l[g], 1e-12f);
+            A.att[(int64_t)(hk * G + g) * D + c] = O / fmaxf(Ls, 1e-12f);
           } else {
-            part[g * (D + 2) + 2 + c] = o;
+            part[g * (D + 2) + 2 + c] = O;
             if (c == 0) {
-              part[g * (D + 2)] = st.m[g];
-              part[g * (D + 2) + 1] = st.l[g];
+              part[g * (D + 2)] = M;
+              part[g * (D + 2) + 1] = Ls;
             }
           }
         }
@@ -592,20 +631,33 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
           if (gtid == 0) s_last[grp] = atomicAdd(A.attn_cnt + hk, 1) == sp.S - 1;
           named_sync_id(gbar, kGroupThreads);
           if (s_last[grp]) {
+            // the last split of the head merges all S partials: warp g finds g's max and sum and writes
+            // the weights exp(m_q - M) [S][G] over the o area (S <= 8 D), then every thread sums its outputs
             __threadfence();
             const float *hp = A.attn_part + (int64_t)hk * sp.S * G * (D + 2);
-            for (int e = gtid; e < G * D; e += kGroupThreads) {
-              const int g = e / D, c = e % D;
+            float *wq = wo;
+            if (gw < G) {
+              const int g = gw;
               float M = -INFINITY;
-              for (int q = 0; q < sp.S; ++q) M = fmaxf(M, __ldcg(hp + (q * G + g) * (D + 2)));
-              float Ls = 0.0f, O = 0.0f;
-              for (int q = 0; q < sp.S; ++q) {
+              for (int q = lane; q < sp.S; q += 32) M = fmaxf(M, __ldcg(hp + (q * G + g) * (D + 2)));
+              M = warp_max(M);
+              float Ls = 0.0f;
+              for (int q = lane; q < sp.S; q += 32) {
                 const float mq = __ldcg(hp + (q * G + g) * (D + 2));
                 const float e2 = mq == -INFINITY ? 0.0f : expf(mq - M);
-                Ls += __ldcg(hp + (q * G + g) * (D + 2) + 1) * e2;
-                O += __ldcg(hp + (q * G + g) * (D + 2) + 2 + c) * e2;
+                wq[q * G + g] = e2;
+                Ls = fmaf(__ldcg(hp + (q * G + g) * (D + 2) + 1), e2, Ls);
               }
-              A.att[(int64_t)(hk * G + g) * D + c] = O / fmaxf(Ls, 1e-12f);
+              Ls = warp_sum(Ls);
+              if (lane == 0) wml[g] = 1.0f / fmaxf(Ls, 1e-12f);
+            }
+            named_sync_id(gbar, kGroupThreads);
+            for (int e = gtid; e < G * D; e += kGroupThreads) {
+              const int g = e / D, c = e % D;
+              float O = 0.0f;
+#pragma unroll 4
+              for (int q = 0; q < sp.S; ++q) O = fmaf(__ldcg(hp + (q * G + g) * (D + 2) + 2 + c), wq[q * G + g], O);
+              A.att[(int64_t)(hk * G + g) * D + c] = O * wml[g];
             }
             if (gtid == 0) A.attn_cnt[hk] = 0;  // ready for the next layer
           }
@@ -720,7 +772,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
 namespace {
 template <int D, int G>
 size_t step_attn_floats() {
-  return (size_t)kStepGroups * AttnCfg<D, G>::SM_END + (size_t)kStepGroups * D;  // + one-key tiles (2 D halves)
+  return (size_t)kStepGroups * AttnCfg<D, G>::SM_END;
 }
 template <int D, int G>
 const void *step_kernel(bool tp) {
