@@ -68,11 +68,17 @@ fg_handle Ctx::add(const Tensor &t) {
   return h;
 }
 
-Tensor &Ctx::get(fg_handle h) {
+Tensor &Ctx::peek(fg_handle h) {
   if (h != 0 && (h >> 40) != epoch) raise(FG_ERR_STALE_HANDLE, "Stale tensor handle from a previous device: tensor_%llx", (unsigned long long)h);
   auto it = tensors.find(h);
   if (it == tensors.end()) raise(FG_ERR_DISPOSED, "Tensor not found: tensor_%llx", (unsigned long long)h);
   return it->second;
+}
+
+Tensor &Ctx::get(fg_handle h) {
+  Tensor &t = peek(h);
+  if (t.lazy) materialize(h, t);
+  return t;
 }
 
 fg_handle Ctx::make(const int64_t *shape, int ndim, int dtype, Tensor **out) {
@@ -95,6 +101,18 @@ void Ctx::dispose(fg_handle h) {
   if (h == 0 || (h >> 40) != epoch) return;
   auto it = tensors.find(h);
   if (it == tensors.end()) return;  // double dispose is a no-op (tensorRegistry.ts:137-139)
+  // lazy tensors that read h take their values now
+  std::vector<fg_handle> users;
+  for (auto r = lazy_users.equal_range(h); r.first != r.second; ++r.first) users.push_back(r.first->second);
+  for (fg_handle u : users) get(u);
+  it = tensors.find(h);
+  if (it->second.lazy) {  // an unread lazy tensor: drop its link to the source
+    for (auto r = lazy_users.equal_range(it->second.lazy->src); r.first != r.second; ++r.first)
+      if (r.first->second == h) {
+        lazy_users.erase(r.first);
+        break;
+      }
+  }
   free_async(it->second.ptr, it->second.bytes);
   tensors.erase(it);
 }
@@ -345,7 +363,9 @@ int fg_shutdown(fg_ctx *ctx) {
     Ctx &c = ctx->c;
     cudaSetDevice(c.device);
     cudaStreamSynchronize(c.stream);
-    for (auto &kv : c.tensors) cudaFreeAsync(kv.second.ptr, c.stream);
+    for (auto &kv : c.tensors)
+      if (kv.second.ptr) cudaFreeAsync(kv.second.ptr, c.stream);
+    c.lazy_users.clear();
     if (c.gemv.part) cudaFreeAsync(c.gemv.part, c.stream);
     if (c.gemv.xh) cudaFreeAsync(c.gemv.xh, c.stream);
     c.tensors.clear();

@@ -97,7 +97,9 @@ __global__ void __launch_bounds__(256) k_qgemm_simt(QMat w, const float *__restr
   }
 }
 
-// Dense fp32 C = A B (matmul_tiled.wgsl.ts semantics, edges zero-padded).
+// Dense fp32 C = A B (matmul_tiled.wgsl.ts semantics, edges zero-padded).  BT: B is stored
+// transposed, [N, K] row-major (nn.Linear's x W^T without materialising W^T).
+template <bool BT>
 __global__ void __launch_bounds__(256) k_matmul_f32(const float *__restrict__ A, const float *__restrict__ B,
                                                     float *__restrict__ C, int64_t M, int64_t K, int64_t N) {
   __shared__ __align__(16) float as[16][BM + 4];
@@ -112,8 +114,13 @@ __global__ void __launch_bounds__(256) k_matmul_f32(const float *__restrict__ A,
       as[k][r] = (m0 + r < M && k0 + k < K) ? A[(m0 + r) * K + k0 + k] : 0.0f;
     }
     for (int idx = tid; idx < BN * 16; idx += 256) {
-      const int k = idx / BN, c = idx % BN;
-      bs[k][c] = (n0 + c < N && k0 + k < K) ? B[(k0 + k) * N + n0 + c] : 0.0f;
+      if constexpr (BT) {  // consecutive threads walk K: coalesced rows of B^T
+        const int c = idx / 16, k = idx % 16;
+        bs[k][c] = (n0 + c < N && k0 + k < K) ? B[(n0 + c) * K + k0 + k] : 0.0f;
+      } else {
+        const int k = idx / BN, c = idx % BN;
+        bs[k][c] = (n0 + c < N && k0 + k < K) ? B[(k0 + k) * N + n0 + c] : 0.0f;
+      }
     }
     __syncthreads();
 #pragma unroll
@@ -166,10 +173,14 @@ void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilo
   FG_CUDA(cudaLaunchKernelEx(&cfg, k_qgemm_simt, w, x, ldx, M, ep));
 }
 
-void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s) {
+void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s,
+                       bool b_trans) {
   if (M == 0 || N == 0) return;
   dim3 grid((unsigned)ceil_div(N, BN), (unsigned)ceil_div(M, BM));
-  k_matmul_f32<<<grid, 256, 0, s>>>(A, B, C, M, K, N);
+  if (b_trans)
+    k_matmul_f32<true><<<grid, 256, 0, s>>>(A, B, C, M, K, N);
+  else
+    k_matmul_f32<false><<<grid, 256, 0, s>>>(A, B, C, M, K, N);
   FG_LAUNCH_CHECK();
 }
 

@@ -1,6 +1,7 @@
 // Context, tensor registry, allocator and kernel launcher declarations.
 #pragma once
 
+#include <memory>
 #include <mutex>
 #include <unordered_map>
 #include <vector>
@@ -11,7 +12,33 @@ struct ncclComm;
 
 namespace fg {
 
+struct Ctx;
+
+// A float32 [B, H, cap, d] buffer of the graph front-end's key/value tensors: the first `tip`
+// positions of every (b, h) are written; tensors over it see their first `len` positions.  An
+// append to the tensor whose len == tip writes in place (the reference re-concatenates the
+// whole cache every step).  Freed through the context when the last tensor over it goes.
+struct KVStore {
+  Ctx *ctx = nullptr;
+  float *ptr = nullptr;
+  uint64_t bytes = 0;
+  int64_t B = 0, H = 0, cap = 0, d = 0, tip = 0;
+  ~KVStore();
+};
+
+// A tensor of the graph front-end that is not materialised yet: its value is a pure function of the
+// tensor `src` (kept readable by the context: disposing `src` first materialises its lazy users),
+// or of a key/value store.
+struct LazyView {
+  enum Kind { T2D = 1, HEADS = 2, KVCAP = 3 } kind = T2D;
+  uint64_t src = 0;            // handle of the source tensor (T2D, HEADS)
+  std::vector<int32_t> heads;  // HEADS: head j of this [B, H, S, d] tensor is head heads[j] of src
+  std::shared_ptr<KVStore> store;  // KVCAP: this tensor is positions [0, len) of the store
+  int64_t len = 0;
+};
+
 struct Tensor {
+  std::shared_ptr<LazyView> lazy;  // set: ptr is null until the first get()
   void *ptr = nullptr;
   uint64_t bytes = 0;
   int32_t dtype = FG_F32;
@@ -41,6 +68,13 @@ struct GemvScratch {
   uint64_t xh_elems = 0;
 };
 
+// Graph limits of configureRuntime (graphExecutor.ts:98-116, defaults as there).
+struct GraphLimits {
+  int64_t max_instructions = 10000;
+  int max_shape_dim = 8;
+  int64_t max_elements = 256ll * 1024 * 1024;
+};
+
 // One context = one device, one stream, one handle namespace (the reference's
 // _globalRegistry + QuotaManager + device singleton, per GPU).
 struct Ctx {
@@ -55,6 +89,7 @@ struct Ctx {
   uint64_t epoch = 1;  // bumped on context loss; handles of an old epoch are stale
   uint64_t limit = 0, active = 0, pending = 0, peak = 0;
   bool allow_non_finite = false;
+  GraphLimits graph;
   bool lost = false;
   // Pinned staging ring for host <-> device copies (buffers.ts:70-140 keeps a
   // pow-2 staging pool; here two pinned halves alternate so the host copy of
@@ -69,7 +104,10 @@ struct Ctx {
   void *alloc(uint64_t bytes);
   void free_async(void *p, uint64_t bytes);
   fg_handle add(const Tensor &t);
-  Tensor &get(fg_handle h);
+  Tensor &get(fg_handle h);   // materialises a lazy tensor
+  Tensor &peek(fg_handle h);  // the registry entry as it is (graph front-end)
+  void materialize(fg_handle h, Tensor &t);  // graph.cu
+  std::unordered_multimap<uint64_t, uint64_t> lazy_users;  // source handle -> lazy tensors reading it
   fg_handle make(const int64_t *shape, int ndim, int dtype, Tensor **out = nullptr);
   void dispose(fg_handle h);
   void h2d(void *dst, const void *src, uint64_t bytes);
@@ -134,7 +172,9 @@ bool qgemm_tc_supported(const QMat &w, int M);
 inline uint64_t tc_xh_elems(int64_t M, int64_t K) { return (uint64_t)M * (uint64_t)(q4_quads(K) * 128); }
 void launch_qgemm_tc(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, const GemvScratch &sc,
                      int num_sms, cudaStream_t s);
-void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s);
+// C[M, N] = A[M, K] B[K, N]; b_trans: B stored as [N, K].
+void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s,
+                       bool b_trans = false);
 
 // attention.cu
 struct AttnArgs {

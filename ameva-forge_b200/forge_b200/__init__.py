@@ -8,7 +8,8 @@ from . import errors
 from ._capi import LIB_PATH, lib
 from .gpu_core import Context, default, device_count, init, nccl_unique_id
 from .gguf import GGUFFile
+from .graph import GraphBuilder, configure_graph, execute_graph
 from .llama import LLAMA2_7B, TINYLLAMA_1_1B, LlamaConfig, LlamaForCausalLM
 
-__all__ = ["errors", "LIB_PATH", "lib", "Context", "default", "device_count", "init", "nccl_unique_id",
+__all__ = ["GraphBuilder", "configure_graph", "execute_graph", "errors", "LIB_PATH", "lib", "Context", "default", "device_count", "init", "nccl_unique_id",
            "GGUFFile", "LlamaConfig", "LlamaForCausalLM", "LLAMA2_7B", "TINYLLAMA_1_1B"]

@@ -104,6 +104,8 @@ _SIGS = {
     "fg_gguf_meta_string": [c_vp, ctypes.c_char_p, P(ctypes.c_char_p)],
     "fg_gguf_llama_config": [c_vp, c_i32, c_i32, P(LlamaConfigC)],
     "fg_llama_load_gguf": [c_vp, c_vp],
+    "fg_execute_graph": [c_vp, ctypes.c_char_p, P(c_vp), P(c_u64), c_i32, P(c_i64), P(c_h), c_i32, P(c_i32)],
+    "fg_configure_graph": [c_vp, c_i64, c_i32, c_i64],
 }
 _RESTYPE = {"fg_version": ctypes.c_char_p, "fg_last_error": ctypes.c_char_p, "fg_status_name": ctypes.c_char_p}
 

@@ -213,6 +213,32 @@ int fg_sample(fg_ctx *ctx, fg_handle logits, double temperature, int32_t top_k, 
 /* Element-type conversion F32 <-> F16 (round to nearest even). */
 int fg_cast(fg_ctx *ctx, fg_handle x, int32_t dtype, fg_handle *out);
 
+/* ---- graph front-end: executeGraph (graphExecutor.ts:487-1979) -------------
+ * Runs the JSON instruction list of forge-py's GraphBuilder (graph.py:26-203):
+ * [{"op", "id", "shape", "in"?, "params"?, "handle"?}, ...].  Validation
+ * follows validateInstruction (graphExecutor.ts:310-478) with its messages
+ * and error classes; the k-th "upload" node takes inputs[k] (float32, exactly
+ * prod(shape) * 4 = input_bytes[k] bytes; non-finite values rejected unless
+ * allowed); a "load" node names an existing tensor as "tensor_<hex handle>"
+ * (or the decimal handle) and may also name F16 / Q4_0 / Q8_0 tensors, which
+ * the Llama path consumes directly (a Q4_0 weight W under transpose -> matmul
+ * runs the fused dequant GEMV / GEMM).  On success out_ids[i] / out_handles[i]
+ * hold every node's id and tensor handle in instruction order (n_out = node
+ * count; out_cap must be at least that).  On failure every tensor the call
+ * created is disposed (the GraphTransaction rollback, :1847-1871).  Some node
+ * tensors (a transpose read only by matmul, GQA head slices / cats read only
+ * by attention) are computed only when first read.  Ops implemented: upload,
+ * load, reshape, transpose, permute, slice, cat, matmul, matmul_tiled,
+ * add/sub/mul/div (broadcasting), relu/neg/exp/log/sigmoid/tanh, rope,
+ * rmsnorm, swiglu, unpack_quant, embedding, flash_attention; the other ops of
+ * the allow-list give FG_ERR_UNSUPPORTED_OP. */
+int fg_execute_graph(fg_ctx *ctx, const char *instructions_json, const void *const *inputs,
+                     const uint64_t *input_bytes, int32_t n_inputs, int64_t *out_ids, fg_handle *out_handles,
+                     int32_t out_cap, int32_t *n_out);
+/* configureRuntime({maxInstructions, maxShapeDim, maxElements})
+ * (graphExecutor.ts:98-127); defaults 10000, 8, 2^28. */
+int fg_configure_graph(fg_ctx *ctx, int64_t max_instructions, int32_t max_shape_dim, int64_t max_elements);
+
 /* ---- seeded synthetic data (new; the benchmark inputs) ---------------------
  * value i = mean + std * N01(seed, offset + i), N01 = splitmix64 counter
  * generator feeding a 4-term central-limit normal; dtype F32 or F16. */
