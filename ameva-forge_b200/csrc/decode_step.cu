@@ -130,7 +130,10 @@ struct AttnSplit {
 __device__ __forceinline__ AttnSplit attn_split(int npos, int Hkv, int P) {
   AttnSplit a;
   a.nt = (npos + kKeysPerTile - 1) / kKeysPerTile;
-  a.S = max(1, min(min(P / Hkv, 512), a.nt));  // <= 512: the merge weights [S][G] fit the 8 G D o area
+  // splits per head: enough units for every group, but at least ~4 tiles per unit (a split's fixed cost
+  // -- q load, first-tile latency, its share of the merge -- outweighs fewer tiles); <= 512 so the merge
+  // weights [S][G] fit the 8 G D o area
+  a.S = max(1, min(min(P / Hkv, 512), max(1, a.nt / 4)));
   a.units = Hkv * a.S;
   return a;
 }
@@ -655,7 +658,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
             for (int e = gtid; e < G * D; e += kGroupThreads) {
               const int g = e / D, c = e % D;
               float O = 0.0f;
-#pragma unroll 4
+#pragma unroll 8
               for (int q = 0; q < sp.S; ++q) O = fmaf(__ldcg(hp + (q * G + g) * (D + 2) + 2 + c), wq[q * G + g], O);
               A.att[(int64_t)(hk * G + g) * D + c] = O * wml[g];
             }
