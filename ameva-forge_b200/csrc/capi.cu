@@ -32,6 +32,9 @@ uint64_t dtype_bytes(int dtype, int64_t numel, const int64_t *shape, int ndim) {
     case FG_Q8_0:
       FG_REQUIRE(ndim == 2 && shape[1] % 32 == 0, FG_ERR_SHAPE, "quantized tensors are [rows, cols] with cols %% 32 == 0");
       return qmat_bytes(dtype, shape[0], shape[1]);
+    case FG_Q4_K:
+      FG_REQUIRE(ndim == 2 && shape[1] % 256 == 0, FG_ERR_SHAPE, "Q4_K tensors are [rows, cols] with cols %% 256 == 0");
+      return (uint64_t)shape[0] * (uint64_t)(shape[1] / 256) * 144ull;
     default:
       raise(FG_ERR_DTYPE, "unknown dtype %d", dtype);
   }
@@ -244,7 +247,7 @@ void check_f32(const Tensor &t, const char *what) {
   FG_REQUIRE(t.dtype == FG_F32, FG_ERR_DTYPE, "%s requires float32 tensors", what);
 }
 
-bool is_quant(int dt) { return dt == FG_Q4_0 || dt == FG_Q8_0; }
+bool is_quant(int dt) { return dt == FG_Q4_0 || dt == FG_Q8_0 || dt == FG_Q4_K; }
 
 }  // namespace
 
@@ -449,7 +452,20 @@ int fg_upload_quant(fg_ctx *ctx, int32_t qtype, const void *gguf_blocks, uint64_
   FG_API_BEGIN
   Guard g(ctx);
   Ctx &c = C(ctx);
-  FG_REQUIRE(is_quant(qtype), FG_ERR_DTYPE, "fg_upload_quant: qtype must be Q4_0 or Q8_0");
+  FG_REQUIRE(is_quant(qtype), FG_ERR_DTYPE, "fg_upload_quant: qtype must be Q4_0, Q8_0 or Q4_K");
+  if (qtype == FG_Q4_K) {  // GGUF order on the device: a plain copy
+    FG_REQUIRE(rows >= 0 && cols >= 0 && cols % 256 == 0, FG_ERR_SHAPE,
+               "Q4_K matrix [%lld, %lld]: cols %% 256 != 0", (long long)rows, (long long)cols);
+    const uint64_t need = (uint64_t)rows * (uint64_t)(cols / 256) * 144ull;
+    FG_REQUIRE(bytes == need, FG_ERR_SHAPE, "GGUF payload of %llu bytes, expected %llu", (unsigned long long)bytes,
+               (unsigned long long)need);
+    const int64_t shape[2] = {rows, cols};
+    Tensor *t = nullptr;
+    const fg_handle h = c.make(shape, 2, qtype, &t);
+    if (need) c.h2d(t->ptr, gguf_blocks, need);
+    *out = h;
+    return FG_OK;
+  }
   FG_REQUIRE(rows >= 0 && cols >= 0 && cols % 32 == 0, FG_ERR_SHAPE, "quantized matrix [%lld, %lld]: cols %% 32 != 0",
              (long long)rows, (long long)cols);
   const uint64_t need = (uint64_t)rows * (uint64_t)(cols / 32) * (uint64_t)gguf_block_bytes(qtype);
@@ -493,6 +509,12 @@ int fg_read_quant_gguf(fg_ctx *ctx, fg_handle h, void *host, uint64_t bytes) {
   Ctx &c = C(ctx);
   Tensor &t = c.get(h);
   FG_REQUIRE(is_quant(t.dtype), FG_ERR_DTYPE, "fg_read_quant_gguf: tensor is not quantized");
+  if (t.dtype == FG_Q4_K) {
+    FG_REQUIRE(bytes == t.bytes, FG_ERR_SHAPE, "GGUF read of %llu bytes, expected %llu", (unsigned long long)bytes,
+               (unsigned long long)t.bytes);
+    if (bytes) c.d2h(host, t.ptr, bytes);
+    return FG_OK;
+  }
   const uint64_t need = (uint64_t)t.shape[0] * (uint64_t)(t.shape[1] / 32) * (uint64_t)gguf_block_bytes(t.dtype);
   FG_REQUIRE(bytes == need, FG_ERR_SHAPE, "GGUF read of %llu bytes, expected %llu", (unsigned long long)bytes,
              (unsigned long long)need);
@@ -562,7 +584,16 @@ int fg_dequant(fg_ctx *ctx, fg_handle w, fg_handle *out) {
   Guard g(ctx);
   Ctx &c = C(ctx);
   Tensor &t = c.get(w);
-  FG_REQUIRE(is_quant(t.dtype), FG_ERR_DTYPE, "dequant: tensor is not Q4_0/Q8_0");
+  FG_REQUIRE(is_quant(t.dtype), FG_ERR_DTYPE, "dequant: tensor is not Q4_0/Q8_0/Q4_K");
+  if (t.dtype == FG_Q4_K) {
+    const int64_t shp[2] = {t.shape[0], t.shape[1]};
+    const void *src = t.ptr;
+    Tensor *o = nullptr;
+    const fg_handle h = c.make(shp, 2, FG_F32, &o);
+    launch_dequant_q4k(src, shp[0] * shp[1] / 256, (float *)o->ptr, c.stream);
+    *out = h;
+    return FG_OK;
+  }
   const QMat q = t.qmat();
   const int64_t shp[2] = {q.N, q.K};
   Tensor *o = nullptr;
@@ -576,13 +607,22 @@ namespace {
 // Validates x [..., K] against W [N, K]; returns M (rows of x).
 int64_t qmatmul_rows(const Tensor &xt, const Tensor &wt) {
   check_f32(xt, "qmatmul activations");
-  FG_REQUIRE(is_quant(wt.dtype), FG_ERR_DTYPE, "qmatmul: weight must be Q4_0/Q8_0");
+  FG_REQUIRE(is_quant(wt.dtype), FG_ERR_DTYPE, "qmatmul: weight must be Q4_0/Q8_0/Q4_K");
   const int64_t K = wt.shape[1];
   FG_REQUIRE(xt.ndim >= 1 && xt.shape[xt.ndim - 1] == K, FG_ERR_SHAPE, "qmatmul: x[..., %lld] vs W[%lld, %lld]",
              (long long)(xt.ndim ? xt.shape[xt.ndim - 1] : 0), (long long)wt.shape[0], (long long)K);
   const int64_t M = K ? xt.numel() / K : 0;
   FG_REQUIRE(M <= INT32_MAX, FG_ERR_SHAPE, "qmatmul: too many rows");
   return M;
+}
+
+// Q4_K: GEMV for M <= 8, else the matrix dequantised into a temporary and the fp32 GEMM.
+void qmatmul_q4k(Ctx &c, const Tensor &xt, const Tensor &wt, int64_t M, float *y) {
+  const int64_t N = wt.shape[0], K = wt.shape[1];
+  float *scratch = nullptr;
+  if (M > 8 && N * K) scratch = (float *)c.alloc(4ull * (uint64_t)(N * K));
+  launch_qmatmul_q4k(wt.ptr, N, K, (const float *)xt.ptr, M, y, scratch, c.stream);
+  if (scratch) c.free_async(scratch, 4ull * (uint64_t)(N * K));
 }
 
 void qmatmul_launch(Ctx &c, const Tensor &xt, const QMat &q, int64_t M, float *y) {
@@ -607,13 +647,15 @@ int fg_qmatmul(fg_ctx *ctx, fg_handle x, fg_handle w, fg_handle *out) {
   Tensor &xt = c.get(x);
   Tensor &wt = c.get(w);
   const int64_t M = qmatmul_rows(xt, wt);
-  const QMat q = wt.qmat();
   int64_t shp[FG_MAX_DIMS];
   for (int i = 0; i < xt.ndim; ++i) shp[i] = xt.shape[i];
-  shp[xt.ndim - 1] = q.N;
+  shp[xt.ndim - 1] = wt.shape[0];
   Tensor *o = nullptr;
   const fg_handle h = c.make(shp, xt.ndim, FG_F32, &o);
-  qmatmul_launch(c, c.get(x), q, M, (float *)o->ptr);
+  if (c.get(w).dtype == FG_Q4_K)
+    qmatmul_q4k(c, c.get(x), c.get(w), M, (float *)o->ptr);
+  else
+    qmatmul_launch(c, c.get(x), c.get(w).qmat(), M, (float *)o->ptr);
   *out = h;
   FG_API_END
 }
@@ -626,10 +668,12 @@ int fg_qmatmul_into(fg_ctx *ctx, fg_handle x, fg_handle w, fg_handle out) {
   Tensor &wt = c.get(w);
   Tensor &ot = c.get(out);
   const int64_t M = qmatmul_rows(xt, wt);
-  const QMat q = wt.qmat();
-  FG_REQUIRE(ot.dtype == FG_F32 && ot.numel() == M * q.N, FG_ERR_SHAPE, "qmatmul_into: output must be F32 [.., %lld]",
-             (long long)q.N);
-  qmatmul_launch(c, xt, q, M, (float *)ot.ptr);
+  FG_REQUIRE(ot.dtype == FG_F32 && ot.numel() == M * wt.shape[0], FG_ERR_SHAPE,
+             "qmatmul_into: output must be F32 [.., %lld]", (long long)wt.shape[0]);
+  if (wt.dtype == FG_Q4_K)
+    qmatmul_q4k(c, xt, wt, M, (float *)ot.ptr);
+  else
+    qmatmul_launch(c, xt, wt.qmat(), M, (float *)ot.ptr);
   FG_API_END
 }
 
@@ -871,7 +915,7 @@ int fg_synth_quant(fg_ctx *ctx, int32_t qtype, int64_t rows, int64_t cols, uint6
   FG_API_BEGIN
   Guard g(ctx);
   Ctx &c = C(ctx);
-  FG_REQUIRE(is_quant(qtype), FG_ERR_DTYPE, "synth_quant: qtype must be Q4_0 or Q8_0");
+  FG_REQUIRE(qtype == FG_Q4_0 || qtype == FG_Q8_0, FG_ERR_DTYPE, "synth_quant: qtype must be Q4_0 or Q8_0");
   const int64_t shp[2] = {rows, cols};
   Tensor *o = nullptr;
   const fg_handle h = c.make(shp, 2, qtype, &o);

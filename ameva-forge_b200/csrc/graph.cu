@@ -437,7 +437,7 @@ fg_handle Exec::exec_node(size_t i, const void *const *inputs, const uint64_t *i
                (long long)N, (long long)B, (long long)n.numel);
     const fg_handle src = in_h(n, 0);
     Tensor &a = c.peek(src);
-    const bool quant = a.dtype == FG_Q4_0 || a.dtype == FG_Q8_0;
+    const bool quant = a.dtype == FG_Q4_0 || a.dtype == FG_Q8_0 || a.dtype == FG_Q4_K;
     if (B == 1 && !a.lazy && (quant || (a.dtype == FG_F32 && consumers_only(i, {"matmul"})))) {
       FG_REQUIRE(quant ? (a.shape[0] == M && a.shape[1] == N) : a.numel() == M * N, FG_ERR_SHAPE,
                  "transpose input does not hold [%lld, %lld]", (long long)M, (long long)N);
@@ -474,11 +474,12 @@ fg_handle Exec::exec_node(size_t i, const void *const *inputs, const uint64_t *i
       Tensor &w = c.get(hw);
       FG_REQUIRE(w.shape[0] == N && w.numel() == N * K, FG_ERR_SHAPE, "%s: transposed B must come from [%lld, %lld]",
                  op.c_str(), (long long)N, (long long)K);
-      if (w.dtype == FG_Q4_0 || w.dtype == FG_Q8_0) {
+      if (w.dtype == FG_Q4_0 || w.dtype == FG_Q8_0 || w.dtype == FG_Q4_K) {
         // x is [M, K]: give the activation tensor that shape for the quantized GEMV / GEMM
         FG_REQUIRE(a.ndim == 2 || M * K == 0 || a.shape[a.ndim - 1] == K, FG_ERR_SHAPE, "%s: A rows", op.c_str());
         fg_handle h = 0;
-        return adopt(fg_qmatmul(ctx, ha, hw, &h), h, n);
+        const int st = fg_qmatmul(ctx, ha, hw, &h);
+        return adopt(st, h, n);
       }
       FG_REQUIRE(w.dtype == FG_F32, FG_ERR_DTYPE, "%s: B must be float32", op.c_str());
       const float *ap = (const float *)c.get(ha).ptr, *wp = (const float *)w.ptr;
@@ -745,7 +746,8 @@ fg_handle Exec::exec_node(size_t i, const void *const *inputs, const uint64_t *i
     const int bits = (int)param(n, 0, 4);
     const int64_t gs = (int64_t)param(n, 1, 128);
     fg_handle h = 0;
-    return adopt(fg_unpack_quant(ctx, in_h(n, 0), in_h(n, 1), in_h(n, 2), bits, gs, n.numel, &h), h, n);
+    const int st = fg_unpack_quant(ctx, in_h(n, 0), in_h(n, 1), in_h(n, 2), bits, gs, n.numel, &h);
+    return adopt(st, h, n);
   }
   if (op == "embedding") {  // graphExecutor.ts:1324-1338; params [tokens, dim, vocab, 0]
     FG_REQUIRE(!n.shape.empty(), FG_ERR_SHAPE, "embedding needs at least one dimension");
@@ -886,9 +888,12 @@ void Ctx::materialize(fg_handle h, Tensor &t) {
     const int64_t M = src.shape[0], N = src.ndim == 2 ? src.shape[1] : (M ? src.numel() / M : 0);
     const float *sp = (const float *)src.ptr;
     float *tmp = nullptr;
-    if (src.dtype == FG_Q4_0 || src.dtype == FG_Q8_0) {  // dequantise, then transpose
+    if (src.dtype == FG_Q4_0 || src.dtype == FG_Q8_0 || src.dtype == FG_Q4_K) {  // dequantise, then transpose
       tmp = (float *)alloc(4ull * (uint64_t)src.numel());
-      launch_dequant(src.qmat(), tmp, stream);
+      if (src.dtype == FG_Q4_K)
+        launch_dequant_q4k(src.ptr, src.numel() / 256, tmp, stream);
+      else
+        launch_dequant(src.qmat(), tmp, stream);
       sp = tmp;
     }
     if (n) {

@@ -1,0 +1,144 @@
+// GGUF Q4_K: dequantisation and the fused dequant-GEMV / GEMM.
+//
+// Q4_K is the super-block format of llama.cpp's Q4_K_M files (ggml's
+// published block_q4_K; the reference's quant path stops at its 4/8-bit
+// unpack, so this extends it): 256 values in 8 sub-blocks of 32, 144 bytes =
+// fp16 d, fp16 dmin, 12 bytes of 6-bit (scale, min) pairs, 128 bytes of
+// nibbles; bytes 32c..32c+31 of the nibbles hold sub-block 2c (low nibbles)
+// and 2c+1 (high nibbles).  value = (d * scale) * q - (dmin * min), two fp32
+// products and one subtraction, rounded separately (no contraction), so the
+// dequantised values are bit-identical to the CPU restatement.
+//
+// On the device the blocks stay in their GGUF order, row-major [N][K / 256]
+// (144 = 9 x 16 bytes: every block starts 16-byte aligned).
+//
+// GEMV (M <= 8 activation rows): one warp per weight row.  Lane l takes the
+// 4-byte nibble word l of each super-block -- sub-blocks 2(l/8) and
+// 2(l/8) + 1, positions 4(l % 8) .. +3 -- so a warp reads the 128 nibble
+// bytes as one coalesced 128-byte line plus the 16-byte header; the scale
+// and min apply per lane before the one warp reduction at the end of the
+// row.  HBM-bound: 144 bytes per 256 weights.  Larger M dequantises the
+// matrix once and runs the fp32 GEMM.
+#include "runtime.cuh"
+
+namespace fg {
+namespace {
+
+__device__ __forceinline__ void q4k_scale_min(int j, const uint8_t *s, int &sc, int &m) {
+  if (j < 4) {
+    sc = s[j] & 63;
+    m = s[j + 4] & 63;
+  } else {
+    sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+    m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+// One thread per (super-block, nibble byte): two values.
+__global__ void k_dequant_q4k(const uint8_t *__restrict__ blocks, int64_t n_blocks, float *__restrict__ out) {
+  const int64_t n = n_blocks * 128;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = t >> 7;
+    const int byte = (int)(t & 127), c = byte >> 5, l = byte & 31;
+    const uint8_t *blk = blocks + b * 144;
+    const float d = __half2float(__ushort_as_half((unsigned short)(blk[0] | (blk[1] << 8))));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(blk[2] | (blk[3] << 8))));
+    int s0, m0, s1, m1;
+    q4k_scale_min(2 * c, blk + 4, s0, m0);
+    q4k_scale_min(2 * c + 1, blk + 4, s1, m1);
+    const uint8_t q = blk[16 + byte];
+    float *o = out + b * 256 + 64 * c + l;
+    o[0] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s0), (float)(q & 0xF)), __fmul_rn(dmin, (float)m0));
+    o[32] = __fsub_rn(__fmul_rn(__fmul_rn(d, (float)s1), (float)(q >> 4)), __fmul_rn(dmin, (float)m1));
+  }
+}
+
+constexpr int kQ4kWarps = 8;
+
+template <int M>
+__global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q4k(const uint8_t *__restrict__ w, int64_t N, int64_t K,
+                                                             const float *__restrict__ x, int64_t ldx,
+                                                             float *__restrict__ y, int64_t ldy) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kQ4kWarps + (threadIdx.x >> 5);
+  if (row >= N) return;
+  const int64_t nb = K / 256;
+  const uint8_t *wr = w + row * nb * 144;
+  const int c = lane >> 3, p = 4 * (lane & 7);
+  float acc[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+#pragma unroll 2
+  for (int64_t b = 0; b < nb; ++b) {
+    const uint8_t *blk = wr + b * 144;
+    const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(blk));  // d, dmin, scales
+    const uint32_t qw = __ldg(reinterpret_cast<const uint32_t *>(blk + 16) + lane);
+    const uint8_t *hb = reinterpret_cast<const uint8_t *>(&hdr);
+    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+    int s0, m0, s1, m1;
+    q4k_scale_min(2 * c, hb + 4, s0, m0);
+    q4k_scale_min(2 * c + 1, hb + 4, s1, m1);
+    const float d0 = d * (float)s0, mm0 = dmin * (float)m0, d1 = d * (float)s1, mm1 = dmin * (float)m1;
+    float lo[4], hi[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      lo[e] = (float)((qw >> (8 * e)) & 0xF);
+      hi[e] = (float)((qw >> (8 * e + 4)) & 0xF);
+    }
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const float *xb = x + m * ldx + b * 256 + 64 * c + p;
+      const float4 xa = __ldg(reinterpret_cast<const float4 *>(xb));
+      const float4 xc = __ldg(reinterpret_cast<const float4 *>(xb + 32));
+      const float qa = lo[0] * xa.x + lo[1] * xa.y + lo[2] * xa.z + lo[3] * xa.w;
+      const float sa = xa.x + xa.y + xa.z + xa.w;
+      const float qc = hi[0] * xc.x + hi[1] * xc.y + hi[2] * xc.z + hi[3] * xc.w;
+      const float sc = xc.x + xc.y + xc.z + xc.w;
+      acc[m] += (d0 * qa - mm0 * sa) + (d1 * qc - mm1 * sc);
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const float v = warp_sum(acc[m]);
+    if (lane == 0) y[m * ldy + row] = v;
+  }
+}
+
+template <int M>
+void gemv_q4k_launch(const uint8_t *w, int64_t N, int64_t K, const float *x, float *y, cudaStream_t s) {
+  k_gemv_q4k<M><<<(unsigned)ceil_div(N, kQ4kWarps), kQ4kWarps * 32, 0, s>>>(w, N, K, x, K, y, N);
+  FG_LAUNCH_CHECK();
+}
+
+}  // namespace
+
+void launch_dequant_q4k(const void *blocks, int64_t n_blocks, float *out, cudaStream_t s) {
+  if (n_blocks == 0) return;
+  const int64_t n = n_blocks * 128;
+  k_dequant_q4k<<<(unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 32), 256, 0, s>>>((const uint8_t *)blocks,
+                                                                                        n_blocks, out);
+  FG_LAUNCH_CHECK();
+}
+
+// y[M, N] = x[M, K] W^T, W Q4_K [N, K]; `scratch` (N K floats) is used when M > 8.
+void launch_qmatmul_q4k(const void *w, int64_t N, int64_t K, const float *x, int64_t M, float *y, float *scratch,
+                        cudaStream_t s) {
+  if (M == 0 || N == 0) return;
+  const uint8_t *wb = (const uint8_t *)w;
+  switch (M) {
+    case 1: return gemv_q4k_launch<1>(wb, N, K, x, y, s);
+    case 2: return gemv_q4k_launch<2>(wb, N, K, x, y, s);
+    case 3: return gemv_q4k_launch<3>(wb, N, K, x, y, s);
+    case 4: return gemv_q4k_launch<4>(wb, N, K, x, y, s);
+    case 5: return gemv_q4k_launch<5>(wb, N, K, x, y, s);
+    case 6: return gemv_q4k_launch<6>(wb, N, K, x, y, s);
+    case 7: return gemv_q4k_launch<7>(wb, N, K, x, y, s);
+    case 8: return gemv_q4k_launch<8>(wb, N, K, x, y, s);
+    default:
+      launch_dequant_q4k(w, N * K / 256, scratch, s);
+      launch_matmul_f32(x, scratch, y, M, K, N, s, /*b_trans=*/true);
+  }
+}
+
+}  // namespace fg

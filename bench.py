@@ -67,6 +67,10 @@ def parse():
     ap.add_argument("--decode-table", action="store_true",
                     help="decode rows of the scope table: TinyLlama-1.1B shape b1 ctx 2048 (256 tokens), "
                          "Llama-2-7B shape b1/16/64 ctx 4096; prints one line per row")
+    ap.add_argument("--graph-decode", action="store_true",
+                    help="the executeGraph path: forge-py's Llama graph (GraphLlama) over TinyLlama-1.1B-shaped "
+                         "Q4_0 weights, a 128-token prompt, then `steps` cached greedy tokens, one graph each "
+                         "(JSON build, parse, run, logits read and host argmax all inside the timing)")
     ap.add_argument("--profile-layers", type=int, default=0,
                     help="profiling case: a model of this many 7B layers at context 4096, `steps` decode steps; "
                          "prints no bench line")
@@ -401,6 +405,55 @@ def decode_table(local, steps, warmup):
     return rows
 
 
+def graph_decode(local, steps, warmup):
+    """Decode through fg_execute_graph, as forge-py's model drives the reference (llama.py:211-248):
+    one instruction list per token built by GraphLlama, the present keys/values passed on as handles.
+    Wall-clock per token (the loop is host-synchronous: every step reads its logits)."""
+    import time
+
+    import forge_b200
+    from forge_b200.graph_llama import GraphLlama
+    from forge_b200.llama import TINYLLAMA_1_1B
+    shape = dict(TINYLLAMA_1_1B)
+    ctx = forge_b200.Context(device=local)
+    m = GraphLlama(ctx, **shape)
+    w = {}
+    for i, name in enumerate(m.weight_names()):
+        shp = m.weight_shape(name)
+        if name == "embed":
+            w[name] = ctx.synth_normal(shp, np.float16, seed=SEED + i, std=0.02)
+        elif len(shp) == 1:
+            w[name] = ctx.synth_normal(shp, np.float32, seed=SEED + i, mean=1.0, std=0.1)
+        else:
+            w[name] = ctx.synth_quant("Q4_0", shp[0], shp[1], seed=SEED + i)
+    m.weights = w
+    prompt = [int(t) for t in (np.arange(128) * 7919 + 11) % shape["vocab_size"]]
+    m.generate(prompt, 1 + warmup)  # prefill + warm-up steps (a run of its own)
+    ctx.synchronize()
+    t0 = time.perf_counter()
+    toks = m.generate(prompt, 1)  # prefill alone, subtracted below
+    ctx.synchronize()
+    t_prefill = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    toks = m.generate(prompt, 1 + steps)
+    ctx.synchronize()
+    dt = time.perf_counter() - t0 - t_prefill
+    g = forge_b200.GraphBuilder()
+    m.forward(g, {}, np.array([prompt]), 0)
+    n_pre = len(g.nodes)
+    g = forge_b200.GraphBuilder()
+    m.forward(g, {}, np.array([[1]]), len(prompt), [(1, 2, len(prompt))] * m.L)  # node count only
+    nodes_step = len(g.nodes)
+    for h in w.values():
+        ctx.dispose(h)
+    ctx.shutdown()
+    return {"decode": "tinyllama-1.1b via executeGraph", "batch": 1, "context": len(prompt), "steps": steps,
+            "tokens_per_s": steps / dt, "ms_per_step": dt / steps * 1e3, "prefill_ms": t_prefill * 1e3,
+            "graph_nodes_per_step": nodes_step, "graph_nodes_prefill": n_pre,
+            "path": "forge-py Llama graph JSON -> fg_execute_graph (transpose fold, Q4_0 fused GEMV, native GQA, "
+                    "in-place KV append); host argmax per token", "tokens": len(toks)}
+
+
 def ctx_stream(ctx):
     import ctypes
     from forge_b200 import _capi as C
@@ -499,6 +552,9 @@ def main():
     if args.decode_table:
         for r in decode_table(local, args.steps, args.warmup):
             print(json.dumps(r), flush=True)
+        return
+    if args.graph_decode:
+        print(json.dumps(graph_decode(local, args.steps, args.warmup)), flush=True)
         return
     if args.attention_case:
         ctx = forge_b200.Context(device=local)

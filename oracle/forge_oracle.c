@@ -294,6 +294,65 @@ FO_EXPORT void fo_qmatmul(int qtype, const uint8_t *blocks, int64_t N, int64_t K
   }
 }
 
+/*
+ * GGUF Q4_K super-block (the published ggml block_q4_K layout of llama.cpp's
+ * Q4_K_M files; no counterpart in the reference, whose quant path is the
+ * 4/8-bit unpack): 256 values in 8 sub-blocks of 32, 144 bytes = fp16 d,
+ * fp16 dmin, 12 bytes of 6-bit (scale, min) pairs, 128 bytes of nibbles.
+ * Bytes 32c..32c+31 of the nibbles hold sub-block 2c (low nibbles) and 2c+1
+ * (high nibbles).  Pair j < 4: scale = s[j] & 63, min = s[j+4] & 63; j >= 4:
+ * scale = (s[j+4] & 15) | (s[j-4] >> 6) << 4, min = (s[j+4] >> 4) | (s[j] >> 6) << 4.
+ * value = (d * scale) * q - (dmin * min): two fp32 products, one subtraction.
+ */
+static inline void fo_q4k_scale_min(int j, const uint8_t *s, int *sc, int *m) {
+  if (j < 4) {
+    *sc = s[j] & 63;
+    *m = s[j + 4] & 63;
+  } else {
+    *sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+    *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+  }
+}
+
+static inline void fo_dequant_q4k_block(const uint8_t *blk, float *out) {
+  const float d = fo_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+  const float dmin = fo_f16_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+  const uint8_t *sc = blk + 4, *qs = blk + 16;
+  for (int c = 0; c < 4; ++c) {
+    int s0, m0, s1, m1;
+    fo_q4k_scale_min(2 * c, sc, &s0, &m0);
+    fo_q4k_scale_min(2 * c + 1, sc, &s1, &m1);
+    const float d0 = d * (float)s0, mm0 = dmin * (float)m0, d1 = d * (float)s1, mm1 = dmin * (float)m1;
+    for (int l = 0; l < 32; ++l) {
+      out[64 * c + l] = d0 * (float)(qs[32 * c + l] & 0xF) - mm0;
+      out[64 * c + 32 + l] = d1 * (float)(qs[32 * c + l] >> 4) - mm1;
+    }
+  }
+}
+
+FO_EXPORT void fo_dequant_q4k(const uint8_t *blocks, int64_t n_blocks, float *out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < n_blocks; ++b) fo_dequant_q4k_block(blocks + 144 * b, out + 256 * b);
+}
+
+/* y[m, n] = sum_k x[m, k] W[n, k], W Q4_K [N, K] dequantised as above; double accumulation. */
+FO_EXPORT void fo_qmatmul_q4k(const uint8_t *blocks, int64_t N, int64_t K, const float *x, int64_t M, float *y) {
+  const int64_t nb = K / 256;
+#pragma omp parallel for schedule(dynamic, 16)
+  for (int64_t n = 0; n < N; ++n) {
+    float wrow[256];
+    for (int64_t m = 0; m < M; ++m) {
+      double acc = 0.0;
+      for (int64_t b = 0; b < nb; ++b) {
+        fo_dequant_q4k_block(blocks + (n * nb + b) * 144, wrow);
+        const float *xr = x + m * K + 256 * b;
+        for (int j = 0; j < 256; ++j) acc += (double)xr[j] * (double)wrow[j];
+      }
+      y[m * N + n] = (float)acc;
+    }
+  }
+}
+
 /* Dense fp32 matmul C[M,N] = A[M,K] B[K,N]: cpuMatMul of
  * packages/forge/tests/matmul_tiled.test.ts:20 (double accumulation). */
 FO_EXPORT void fo_matmul(const float *A, const float *B, int64_t M, int64_t K, int64_t N, float *C) {

@@ -60,6 +60,8 @@ def lib():
         L.fo_unpack_quant.argtypes = [_u32p, _f32p, _f32p, ctypes.c_int, _i64, _i64, _f32p]
         L.fo_dequant.argtypes = [ctypes.c_int, _u8p, _i64, _f32p]
         L.fo_qmatmul.argtypes = [ctypes.c_int, _u8p, _i64, _i64, _f32p, _i64, _f32p]
+        L.fo_dequant_q4k.argtypes = [_u8p, _i64, _f32p]
+        L.fo_qmatmul_q4k.argtypes = [_u8p, _i64, _i64, _f32p, _i64, _f32p]
         L.fo_matmul.argtypes = [_f32p, _f32p, _i64, _i64, _i64, _f32p]
         L.fo_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                    ctypes.c_float, ctypes.c_int]
@@ -149,6 +151,35 @@ def dequant(qtype: int, blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
     out = np.empty((rows, cols), dtype=np.float32)
     lib().fo_dequant(qtype, _p(blocks.reshape(-1), _u8p), rows * cols // 32, _p(out, _f32p))
     return out
+
+
+def dequant_q4k(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """GGUF Q4_K super-blocks [rows, cols / 256 * 144] -> fp32 [rows, cols] (forge_oracle.c)."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty((rows, cols), dtype=np.float32)
+    lib().fo_dequant_q4k(_p(blocks.reshape(-1), _u8p), rows * cols // 256, _p(out, _f32p))
+    return out
+
+
+def qmatmul_q4k(blocks: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M = x.size // K
+    y = np.empty((M, N), dtype=np.float32)
+    lib().fo_qmatmul_q4k(_p(np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1), _u8p), N, K,
+                         _p(x.reshape(-1), _f32p), M, _p(y, _f32p))
+    return y.reshape(x.shape[:-1] + (N,))
+
+
+def random_q4k(rows: int, cols: int, seed: int, d_scale: float = 1e-3) -> np.ndarray:
+    """Random valid Q4_K blocks: finite positive fp16 d / dmin, random 6-bit packs and nibbles."""
+    rng = np.random.default_rng(seed)
+    nb = rows * cols // 256
+    b = rng.integers(0, 256, size=(nb, 144), dtype=np.uint8)
+    d = (rng.random(nb) * d_scale + d_scale / 8).astype(np.float16).view(np.uint16)
+    dm = (rng.random(nb) * d_scale + d_scale / 8).astype(np.float16).view(np.uint16)
+    b[:, 0], b[:, 1] = d & 0xFF, d >> 8
+    b[:, 2], b[:, 3] = dm & 0xFF, dm >> 8
+    return b.reshape(rows, cols // 256 * 144)
 
 
 def qmatmul(qtype: int, blocks: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:

@@ -37,6 +37,7 @@ def test_reference_llama_graph_prefill_and_decode(ctx):
     """The reference model's own 255-node graph (prefill, KV cat-append, GQA repetition, decode step)."""
     z, js, inputs = _load("graph_llama.npz")
     nodes = json.loads(js)
+    _dispose(ctx, _run(ctx, js, inputs))  # first run: the context caches its RoPE frequency table
     ctx.synchronize()
     before = ctx.quota()["active"]
     out = _run(ctx, js, inputs)
@@ -278,3 +279,43 @@ def test_kv_append_in_place_across_calls(ctx):
     assert max_rel_err(ctx.read(a2), O.attention(q, r2, r2, causal=True)) <= 1e-3
     for o, keep in ((o3, ("1",)), (o2, ("1",)), (o1, ())):
         _dispose(ctx, o, keep)
+
+
+@pytest.mark.parametrize("qt", ["Q4_0", "Q8_0"])
+def test_graph_llama_generate_matches_oracle(ctx, qt):
+    """forge-py's model graph (GraphLlama) with GGUF weights loaded by handle: greedy tokens and logits of
+    a cached generation equal the oracle model's (fp32 cache, as the reference keeps)."""
+    from forge_b200.graph_llama import GraphLlama
+    shape = dict(vocab_size=96, hidden_size=64, intermediate_size=96, num_hidden_layers=2, num_attention_heads=4,
+                 num_key_value_heads=2)
+    qtype = O.Q4_0 if qt == "Q4_0" else O.Q8_0
+    w = O.synth_llama(O.LlamaShape(**shape), seed=31, qtype=qtype, std=0.2)
+    m = GraphLlama(ctx, **shape)
+    H, I, kvd = 64, 96, 2 * 16
+    dims = {"q": (H, H), "k": (kvd, H), "v": (kvd, H), "o": (H, H), "gate": (I, H), "up": (I, H), "down": (H, I)}
+    handles = {"embed": ctx.upload(w.embed_f16.view(np.float16)), "norm": ctx.upload(w.norm),
+               "lm_head": ctx.upload_quant(qt, w.lm_head, 96, H)}
+    for l, lw in enumerate(w.layers):
+        for name, (r, c) in dims.items():
+            handles[f"layers.{l}.{name}"] = ctx.upload_quant(qt, lw[name], r, c)
+        handles[f"layers.{l}.attn_norm"] = ctx.upload(lw["attn_norm"])
+        handles[f"layers.{l}.ffn_norm"] = ctx.upload(lw["ffn_norm"])
+    m.weights = handles
+    prompt = [5, 17, 33, 2, 90]
+    m.generate(prompt, 1)  # the context caches its RoPE frequency table
+    ctx.synchronize()
+    before = ctx.quota()["active"]
+    lg = []
+    toks = m.generate(prompt, 4, lg)
+    ctx.synchronize()
+    assert ctx.quota()["active"] == before  # every graph tensor and cache store was released
+    ref = O.LlamaRef(w, max_seq=16, kv_f16=False)
+    ids = np.array([prompt], np.int32)
+    want = []
+    for step in range(4):
+        logits = ref.forward(ids)[0, -1]
+        assert max_rel_err(lg[step], logits) <= 1e-3, step
+        want.append(O.argmax(logits))
+        ids = np.array([[want[-1]]], np.int32)
+    assert toks == prompt + want
+    ctx.dispose_batch(list(handles.values()))

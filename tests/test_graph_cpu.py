@@ -63,3 +63,20 @@ def test_builder_rejects_like_reference():
         g.add_upload((1,) * 9)
     with pytest.raises(ValueError):
         g.add_op("relu", (2,), [0])
+
+
+def test_graph_llama_emits_the_reference_graph():
+    """forge_b200.graph_llama.GraphLlama reproduces forge-py's LlamaForCausalLM graph node for node
+    (prefill of 3 tokens + one cached decode step, weights as uploads on first use)."""
+    import make_graph_golden as M
+    from forge_b200.graph import GraphBuilder
+    from forge_b200.graph_llama import GraphLlama
+    z, js, inputs = _load("graph_llama.npz")
+    m = GraphLlama(None, **M.LLAMA_SHAPE)
+    m.weights = {n: np.zeros(m.weight_shape(n), np.float32) for n in m.weight_names()}
+    g = GraphBuilder()
+    nodes = {}
+    l1, _, present = m.forward(g, nodes, np.array(M.PROMPT), 0)
+    l2, _, _ = m.forward(g, nodes, np.array(M.NEXT), 3, present)
+    assert json.loads(g.compile()[0]) == json.loads(js)
+    assert [l1, l2] == [int(v) for v in z["roots"]]
