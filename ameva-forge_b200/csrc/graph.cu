@@ -965,8 +965,11 @@ extern "C" int fg_execute_graph(fg_ctx *ctx, const char *instructions_json, cons
               in_place_op.c_str(), n.op.c_str());
       }
     }
-    FG_REQUIRE(out_cap >= (int32_t)nodes.size() || !out_ids, FG_ERR_VALIDATION,
-               "executeGraph: output arrays hold %d entries, the graph has %d nodes", out_cap, (int)nodes.size());
+    if (out_ids && out_cap < (int32_t)nodes.size()) {  // nothing has run: report the size needed
+      if (n_out) *n_out = (int32_t)nodes.size();
+      raise(FG_ERR_VALIDATION, "executeGraph: output arrays hold %d entries, the graph has %d nodes", out_cap,
+            (int)nodes.size());
+    }
     // 3. execute; any failure disposes what this call created
     Exec ex(c, ctx, nodes);
     try {

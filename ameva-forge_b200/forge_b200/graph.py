@@ -107,6 +107,17 @@ class GraphBuilder:
         self.nodes.append(node)
         return nid
 
+    def add_trusted(self, op_name: str, shape, in_ids, params=None) -> int:
+        """add_op for emitters whose arguments are already plain ints / floats of an allowed op
+        (GraphLlama): the same node, without the per-element checks."""
+        nid = self.next_id
+        self.next_id += 1
+        node: Dict[str, Any] = {"op": op_name, "id": nid, "shape": list(shape), "in": list(in_ids)}
+        if params is not None:
+            node["params"] = list(params)
+        self.nodes.append(node)
+        return nid
+
     def to_dict(self) -> Dict[str, Any]:
         return {"instructions": self.nodes, "inputs": self.inputs}
 
@@ -124,16 +135,19 @@ def execute_graph(ctx, instructions_json: str, inputs: Optional[Sequence[Any]] =
     n_in = len(arrays)
     ptrs = (ctypes.c_void_p * max(1, n_in))(*[a.ctypes.data for a in arrays])
     sizes = (ctypes.c_uint64 * max(1, n_in))(*[a.nbytes for a in arrays])
-    try:
-        n_nodes = len(json.loads(instructions_json))
-    except (ValueError, TypeError):
-        n_nodes = 0
-    cap = max(1, n_nodes)
-    ids = (ctypes.c_int64 * cap)()
-    hs = (ctypes.c_uint64 * cap)()
-    n_out = ctypes.c_int32(0)
     js = instructions_json.encode("utf-8") if isinstance(instructions_json, str) else instructions_json
-    C.call("fg_execute_graph", ctx.ptr, js, ptrs, sizes, n_in, ids, hs, cap, ctypes.byref(n_out))
+    # every node has an "op" key: the count bounds the node count (the library reports the exact count
+    # without running anything when the arrays are too small, and the call is repeated once)
+    cap = max(1, js.count(b'"op"'))
+    n_out = ctypes.c_int32(0)
+    for _ in range(2):
+        ids = (ctypes.c_int64 * cap)()
+        hs = (ctypes.c_uint64 * cap)()
+        st = C.lib().fg_execute_graph(ctx.ptr, js, ptrs, sizes, n_in, ids, hs, cap, ctypes.byref(n_out))
+        if st == 0 or n_out.value <= cap:
+            break
+        cap = n_out.value
+    C.check(st)
     return {str(ids[i]): "tensor_%016x" % hs[i] for i in range(n_out.value)}
 
 

@@ -75,16 +75,16 @@ class GraphLlama:
         N, K = self.weight_shape(wname)
         lead = tuple(x_shape[:-1])
         flat = int(np.prod(lead))
-        a2 = g.add_op("reshape", (flat, K), [x], [flat, K])
+        a2 = g.add_trusted("reshape", (flat, K), [x], [flat, K])
         w = self._w(g, nodes, wname)
-        t = g.add_op("transpose", (K, N), [w], [N, K])
-        m = g.add_op("matmul", (flat, N), [a2, t], [flat, N, K])
+        t = g.add_trusted("transpose", (K, N), [w], [N, K])
+        m = g.add_trusted("matmul", (flat, N), [a2, t], [flat, N, K])
         out_shape = lead + (N,)
-        return g.add_op("reshape", out_shape, [m], list(out_shape)), out_shape
+        return g.add_trusted("reshape", out_shape, [m], list(out_shape)), out_shape
 
     def _heads(self, g, x: int, B: int, L: int, nh: int) -> int:
-        r = g.add_op("reshape", (B, L, nh, self.hd), [x], [B, L, nh, self.hd])
-        return g.add_op("permute", (B, nh, L, self.hd), [r], [0, 2, 1, 3])
+        r = g.add_trusted("reshape", (B, L, nh, self.hd), [x], [B, L, nh, self.hd])
+        return g.add_trusted("permute", (B, nh, L, self.hd), [r], [0, 2, 1, 3])
 
     def _head_slice(self, g, src: int, B: int, S: int, h: int) -> int:
         """k[:, h:h+1, :, :] (ops.py:2340-2395 params: rank, starts, steps, in/out strides, each padded to 8)."""
@@ -92,7 +92,7 @@ class GraphLlama:
         pad = [0] * 4
         params = ([4] + [0, h, 0, 0] + pad + [1, 1, 1, 1] + pad + [Hkv * S * hd, S * hd, hd, 1] + pad +
                   [S * hd, S * hd, hd, 1] + pad)
-        return g.add_op("slice", (B, 1, S, hd), [src], params)
+        return g.add_trusted("slice", (B, 1, S, hd), [src], params)
 
     def _repeat(self, g, src: int, B: int, S: int) -> int:
         """llama.py:116-127: every KV head G times, concatenated on dim 1 (a left fold of binary cats)."""
@@ -105,7 +105,7 @@ class GraphLlama:
                 if cur is None:
                     cur, n = s, 1
                 else:
-                    cur = g.add_op("cat", (B, n + 1, S, self.hd), [cur, s], [n, 1, S * self.hd])
+                    cur = g.add_trusted("cat", (B, n + 1, S, self.hd), [cur, s], [n, 1, S * self.hd])
                     n += 1
         return cur
 
@@ -117,19 +117,19 @@ class GraphLlama:
         H, hd = self.H, self.hd
         emb = self._w(g, nodes, "embed")
         idn = g.add_upload((B, L), np.ascontiguousarray(ids, dtype=np.float32))
-        h = g.add_op("embedding", (B, L, H), [emb, idn], [B * L, H, self.V, 0])
+        h = g.add_trusted("embedding", (B, L, H), [emb, idn], [B * L, H, self.V, 0])
         shp = (B, L, H)
         present = []
         for l in range(self.L):
             p = f"layers.{l}."
-            normed = g.add_op("rmsnorm", shp, [h, self._w(g, nodes, p + "attn_norm")], [self.eps])
+            normed = g.add_trusted("rmsnorm", shp, [h, self._w(g, nodes, p + "attn_norm")], [self.eps])
             q, _ = self._linear(g, nodes, normed, shp, p + "q")
-            q = g.add_op("rope", (B, self.Hq, L, hd), [self._heads(g, q, B, L, self.Hq)], [self.theta, float(offset)])
+            q = g.add_trusted("rope", (B, self.Hq, L, hd), [self._heads(g, q, B, L, self.Hq)], [self.theta, float(offset)])
             k, _ = self._linear(g, nodes, normed, shp, p + "k")
-            k = g.add_op("rope", (B, self.Hkv, L, hd), [self._heads(g, k, B, L, self.Hkv)], [self.theta, float(offset)])
+            k = g.add_trusted("rope", (B, self.Hkv, L, hd), [self._heads(g, k, B, L, self.Hkv)], [self.theta, float(offset)])
             if past is not None:
                 pk, pv, ps = past[l]
-                k = g.add_op("cat", (B, self.Hkv, ps + L, hd), [pk, k], [ps, L, hd])
+                k = g.add_trusted("cat", (B, self.Hkv, ps + L, hd), [pk, k], [ps, L, hd])
             else:
                 ps = 0
             S = ps + L
@@ -137,22 +137,22 @@ class GraphLlama:
             v, _ = self._linear(g, nodes, normed, shp, p + "v")
             v = self._heads(g, v, B, L, self.Hkv)
             if past is not None:
-                v = g.add_op("cat", (B, self.Hkv, S, hd), [pv, v], [ps, L, hd])
+                v = g.add_trusted("cat", (B, self.Hkv, S, hd), [pv, v], [ps, L, hd])
             vr = self._repeat(g, v, B, S)
             present.append((k, v, S))
-            att = g.add_op("flash_attention", (B, self.Hq, L, hd), [q, kr, vr],
+            att = g.add_trusted("flash_attention", (B, self.Hq, L, hd), [q, kr, vr],
                            [float(self.Hq), 1.0 / math.sqrt(hd), 1.0, float(S)])
-            att = g.add_op("permute", (B, L, self.Hq, hd), [att], [0, 2, 1, 3])
-            att = g.add_op("reshape", shp, [att], list(shp))
+            att = g.add_trusted("permute", (B, L, self.Hq, hd), [att], [0, 2, 1, 3])
+            att = g.add_trusted("reshape", shp, [att], list(shp))
             o, _ = self._linear(g, nodes, att, shp, p + "o")
-            h = g.add_op("add", shp, [h, o], [B * L * H, B * L * H])
-            nm = g.add_op("rmsnorm", shp, [h, self._w(g, nodes, p + "ffn_norm")], [self.eps])
+            h = g.add_trusted("add", shp, [h, o], [B * L * H, B * L * H])
+            nm = g.add_trusted("rmsnorm", shp, [h, self._w(g, nodes, p + "ffn_norm")], [self.eps])
             gate, gshp = self._linear(g, nodes, nm, shp, p + "gate")
             up, _ = self._linear(g, nodes, nm, shp, p + "up")
-            sw = g.add_op("swiglu", gshp, [gate, up])
+            sw = g.add_trusted("swiglu", gshp, [gate, up])
             down, _ = self._linear(g, nodes, sw, gshp, p + "down")
-            h = g.add_op("add", shp, [h, down], [B * L * H, B * L * H])
-        h = g.add_op("rmsnorm", shp, [h, self._w(g, nodes, "norm")], [self.eps])
+            h = g.add_trusted("add", shp, [h, down], [B * L * H, B * L * H])
+        h = g.add_trusted("rmsnorm", shp, [h, self._w(g, nodes, "norm")], [self.eps])
         logits, lshp = self._linear(g, nodes, h, shp, "lm_head")
         return logits, lshp, present
 

@@ -301,7 +301,9 @@ def test_graph_llama_generate_matches_oracle(ctx, qt):
         handles[f"layers.{l}.attn_norm"] = ctx.upload(lw["attn_norm"])
         handles[f"layers.{l}.ffn_norm"] = ctx.upload(lw["ffn_norm"])
     m.weights = handles
-    prompt = [5, 17, 33, 2, 90]
+    # four prompt tokens: every projection runs the GEMV path, whose x digits are exact (longer prompts
+    # take the tensor-core GEMM with fp16 activations; its own tolerance tests are test_gpu_qmatmul's)
+    prompt = [5, 17, 33, 2]
     m.generate(prompt, 1)  # the context caches its RoPE frequency table
     ctx.synchronize()
     before = ctx.quota()["active"]
