@@ -44,25 +44,30 @@ constexpr int kStepThreads = kStepConsumers + kStepGroups * 32;  // + one produc
 constexpr int kKeysPerTile = 32;
 constexpr int kBarConsumers = 3;                                 // named barrier of all consumer warps
 
-enum Phase { PH_EMBED, PH_QKV, PH_ATTN, PH_O, PH_GATEUP, PH_DOWN, PH_LM, PH_ARGMAX, PH_COMB };
+enum Phase { PH_EMBED, PH_QKV, PH_ATTN, PH_O, PH_GATEUP, PH_DOWN, PH_LM, PH_ARGMAX };
 
-// Phases of a layer: QKV, ATTN, O, GATEUP, DOWN; under tensor parallelism (per = 7) O and DOWN
-// produce partial sums that every rank exchanges, and a COMB phase after each adds them to h.
+// Phases of a layer: QKV, ATTN, O, GATEUP, DOWN; under tensor parallelism O and DOWN produce partial
+// sums that every rank exchanges (see fold_index).
 __device__ __forceinline__ Phase phase_kind(int p, int L, int per) {
   if (p == 0) return PH_EMBED;
-  if (p <= per * L) {
-    const int k = (p - 1) % per;
-    if (per == 5) return (Phase)(PH_QKV + k);
-    // QKV, ATTN, O, COMB, GATEUP, DOWN, COMB
-    if (k == 3 || k == 6) return PH_COMB;
-    return (Phase)(PH_QKV + (k < 3 ? k : k - 1));
-  }
+  if (p <= per * L) return (Phase)(PH_QKV + (p - 1) % per);
   return p == per * L + 1 ? PH_LM : PH_ARGMAX;
 }
 // Exchange index within the launch of an O / DOWN phase (or the COMB after it).
 __device__ __forceinline__ int xchg_index(int p, int per) {
   const int l = (p - 1) / per, k = (p - 1) % per;
   return 2 * l + (k >= 4 ? 1 : 0);
+}
+// Tensor parallelism: the phase after an exchange adds the ranks' partial sums to the residual while it
+// stages its input -- GATEUP folds its layer's o_proj exchange 2l, QKV of layer l + 1 and LM the
+// down_proj exchange 2l + 1.  -1: no fold.
+__device__ __forceinline__ int fold_index(int p, int L) {
+  if (p == 5 * L + 1) return 2 * L - 1;
+  if (p < 1 || p > 5 * L) return -1;
+  const int l = (p - 1) / 5, k = (p - 1) % 5;
+  if (k == 3) return 2 * l;
+  if (k == 0 && l > 0) return 2 * l - 1;
+  return -1;
 }
 
 __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
@@ -139,22 +144,6 @@ __device__ __forceinline__ AttnSplit attn_split(int npos, int Hkv, int P) {
 }
 
 }  // namespace
-
-// COMB phase of one group: h[e0, e1) += the partial sums of every rank for exchange xi, in rank order
-// (the same order on every rank, so h stays bit-identical across ranks).  False on a timeout.
-__device__ __noinline__ bool comb_slice(const StepArgs &A, int xi, unsigned long long seq, int e0, int e1, int gtid,
-                                        int gbar, int *s_flag) {
-  if (gtid == 0) *s_flag = wait_peers(A, xflag_words(A, A.rank), seq) ? 0 : -1;
-  named_sync_id(gbar, kGroupThreads);
-  if (*s_flag != 0) return false;
-  const float *part = A.xr[A.rank] + (int64_t)(xi & 1) * A.tp * A.H;
-  for (int e = e0 + gtid; e < e1; e += kGroupThreads) {
-    float v = A.h[e];
-    for (int r = 0; r < A.tp; ++r) v += __ldcg(part + (int64_t)r * A.H + e);
-    A.h[e] = v;
-  }
-  return true;
-}
 
 // The greedy pick over every rank's vocabulary shard: publish this rank's best key to the others,
 // wait for theirs, return the maximum (or `key` unchanged and false on a timeout).
@@ -472,7 +461,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   __shared__ unsigned long long s_key[kStepConsumers / 32];
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  constexpr int per = TP ? 7 : 5;
+  constexpr int per = 5;  // QKV, ATTN, O, GATEUP, DOWN (tensor parallelism folds its exchanges into staging)
   const int L = A.L, nphase = per * L + 3;
   const int P = kStepGroups * gridDim.x;
   unsigned char *rings = base;                                            // [2][stages][18 KB]
@@ -666,12 +655,6 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
           }
         }
       }
-    } else if (TP && ph == PH_COMB) {
-      // h += the partial sums of every rank, in rank order (the same order on every rank, so h stays
-      // bit-identical across ranks); each group owns a slice of h
-      const int xi = xchg_index(p, per);
-      const int e0 = (int)((int64_t)vk * A.H / P), e1 = (int)((int64_t)(vk + 1) * A.H / P);
-      if (e1 > e0) ok = comb_slice(A, xi, xbase * (2 * L) + xi + 1, e0, e1, gtid, gbar, &s_last[grp]);
     } else if (ph == PH_ARGMAX) {
       // slice of the logits -> one key per CTA -> atomicMax (global vocabulary index)
       unsigned long long best = 0;
@@ -711,7 +694,24 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
       const int nq = (int)w.row_words;
       Q4X<1> X;
       X.carve(xarea, (int)(w.K >> 5), nq * 4);
-      q4_stage_x<1>(X, x, w.K, gm, tid, kStepConsumers, s_sum);
+      if constexpr (TP) {
+        const int fx = fold_index(p, L);
+        if (fx >= 0) {
+          // h(out) = h(in) + every rank's partial sums of exchange fx in rank order (the same on every rank,
+          // so h stays bit-identical across ranks); h alternates between two buffers, one per exchange parity
+          if (tid == 0) s_last[0] = wait_peers(A, xflag_words(A, A.rank), xbase * (2 * L) + fx + 1) ? 1 : 0;
+          named_sync_id(kBarConsumers, kStepConsumers);
+          ok = s_last[0] != 0;
+          if (ok)
+            q4_stage_x_fold(X, (fx & 1) ? A.h2 : A.h, A.xr[A.rank] + (int64_t)(fx & 1) * A.tp * A.H, A.tp, A.H,
+                            (fx & 1) ? A.h : A.h2, (int)((int64_t)blockIdx.x * A.H / gridDim.x),
+                            (int)((int64_t)(blockIdx.x + 1) * A.H / gridDim.x), gm, tid, kStepConsumers, s_sum);
+        } else {
+          q4_stage_x<1>(X, x, w.K, gm, tid, kStepConsumers, s_sum);
+        }
+      } else {
+        q4_stage_x<1>(X, x, w.K, gm, tid, kStepConsumers, s_sum);
+      }
       named_sync_id(kBarConsumers, kStepConsumers);
       if (tid == 0) s_inv = rms_inv(s_sum, kStepConsumers / 32, 1, 0, w.K, A.eps, gm != nullptr);
       named_sync_id(kBarConsumers, kStepConsumers);

@@ -267,6 +267,7 @@ void setup_exchange(fg_llama *m) {
     }
   }
   A.xflags = (int64_t)part;
+  A.h2 = (float *)m->dalloc((uint64_t)m->H * 4);
   A.xep = (unsigned long long *)m->dalloc(8);
   FG_CUDA(cudaMemsetAsync(A.xep, 0, 8, c.stream));
   // every rank has zeroed and mapped its region before any rank's step kernel writes into it

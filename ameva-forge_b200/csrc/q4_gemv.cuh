@@ -249,6 +249,81 @@ __device__ __forceinline__ void q4_stage_x(const Q4X<MV> &X, const float *x, int
   }
 }
 
+// q4_stage_x (MV = 1) of the tensor-parallel residual fold: the staged vector is h + parts[0] + ...
+// + parts[np - 1] (in that order), and its elements [s0, s1) are also stored to hout.  K = stride.
+static __device__ __noinline__ void q4_stage_x_fold(const Q4X<1> &X, const float *h, const float *parts, int np,
+                                             int64_t stride, float *hout, int s0, int s1, const float *gamma, int tid,
+                                             int nth, float *ss_out) {
+  const int lane = tid & 31, warp = tid >> 5;
+  const int q = lane & 7;
+  float ss = 0.0f;
+  for (int item = tid; item < X.nbx * 8; item += nth) {
+    const int bb = item >> 3;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (bb < X.nb) {
+      const int k = bb * 32 + 4 * q;
+      v = __ldcg(reinterpret_cast<const float4 *>(h + k));
+      for (int r = 0; r < np; ++r) {
+        const float4 pr = __ldcg(reinterpret_cast<const float4 *>(parts + r * stride + k));
+        v.x += pr.x;
+        v.y += pr.y;
+        v.z += pr.z;
+        v.w += pr.w;
+      }
+      const float e4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (k + i >= s0 && k + i < s1) hout[k + i] = e4[i];
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      if (gamma) {
+        const float4 g = *reinterpret_cast<const float4 *>(gamma + k);
+        v.x *= g.x;
+        v.y *= g.y;
+        v.z *= g.z;
+        v.w *= g.w;
+      }
+    }
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+    const int E = ((__float_as_int(amax) >> 23) & 0xFF) - 127;
+    const int e = min(max(20 - E, -126), 126);
+    const float scl = __int_as_float((e + 127) << 23);
+    const float vf[4] = {v.x, v.y, v.z, v.w};
+    int hi[4], mi[4], lo[4], shi = 0, smi = 0, slo = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int vi = __float2int_rn(fminf(fmaxf(vf[i] * scl, -2097152.0f), 2097151.0f));
+      hi[i] = vi >> 14;
+      mi[i] = (vi >> 7) & 127;
+      lo[i] = vi & 127;
+      shi += hi[i];
+      smi += mi[i];
+      slo += lo[i];
+    }
+    uint32_t *col = reinterpret_cast<uint32_t *>(X.xb + (bb * 3) * 4) + (q & 3) * 2 + (q >> 2);
+    col[0] = pack_s8x4(hi[0], hi[1], hi[2], hi[3]);
+    col[8] = pack_s8x4(mi[0], mi[1], mi[2], mi[3]);
+    col[16] = pack_s8x4(lo[0], lo[1], lo[2], lo[3]);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      shi += __shfl_xor_sync(0xffffffffu, shi, o);
+      smi += __shfl_xor_sync(0xffffffffu, smi, o);
+      slo += __shfl_xor_sync(0xffffffffu, slo, o);
+    }
+    if (q == 0) {
+      X.cx0[bb] = -8 * shi;
+      X.cx1[bb] = -8 * smi;
+      X.cx0[X.nbx + bb] = -8 * slo;
+      X.cx1[X.nbx + bb] = 0;
+      X.fbk[bb] = amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000);
+    }
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) ss_out[warp] = ss;
+}
+
 __device__ __forceinline__ void imma_u8s8(int d[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
                                           uint32_t b1, int c0, int c1) {
   asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%10,%11};"

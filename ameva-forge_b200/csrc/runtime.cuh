@@ -250,6 +250,7 @@ struct StepArgs {
   int64_t xflags = 0;
   unsigned long long *xep = nullptr;  // exchange epoch of this rank (launches; never reset)
   int vocab_l = 0, vbase = 0;         // logits of this rank: vocab_l rows from global index vbase
+  float *h2 = nullptr;                // the residual's second buffer (tensor parallelism: h alternates)
 };
 bool decode_step_supported(int d, int G, int qtype, int64_t H, int64_t I, int64_t qdim);
 size_t decode_step_xarea(int d, int G, int64_t H, int64_t I, int64_t qdim);
