@@ -33,8 +33,9 @@ uint64_t dtype_bytes(int dtype, int64_t numel, const int64_t *shape, int ndim) {
       FG_REQUIRE(ndim == 2 && shape[1] % 32 == 0, FG_ERR_SHAPE, "quantized tensors are [rows, cols] with cols %% 32 == 0");
       return qmat_bytes(dtype, shape[0], shape[1]);
     case FG_Q4_K:
-      FG_REQUIRE(ndim == 2 && shape[1] % 256 == 0, FG_ERR_SHAPE, "Q4_K tensors are [rows, cols] with cols %% 256 == 0");
-      return (uint64_t)shape[0] * (uint64_t)(shape[1] / 256) * 144ull;
+    case FG_Q6_K:
+      FG_REQUIRE(ndim == 2 && shape[1] % 256 == 0, FG_ERR_SHAPE, "k-quant tensors are [rows, cols] with cols %% 256 == 0");
+      return (uint64_t)shape[0] * (uint64_t)(shape[1] / 256) * (dtype == FG_Q4_K ? 144ull : 210ull);
     default:
       raise(FG_ERR_DTYPE, "unknown dtype %d", dtype);
   }
@@ -247,7 +248,9 @@ void check_f32(const Tensor &t, const char *what) {
   FG_REQUIRE(t.dtype == FG_F32, FG_ERR_DTYPE, "%s requires float32 tensors", what);
 }
 
-bool is_quant(int dt) { return dt == FG_Q4_0 || dt == FG_Q8_0 || dt == FG_Q4_K; }
+bool is_kquant(int dt) { return dt == FG_Q4_K || dt == FG_Q6_K; }  // 256-value super-blocks, GGUF order
+bool is_quant(int dt) { return dt == FG_Q4_0 || dt == FG_Q8_0 || is_kquant(dt); }
+uint64_t kquant_block_bytes(int dt) { return dt == FG_Q4_K ? 144 : 210; }
 
 }  // namespace
 
@@ -452,11 +455,11 @@ int fg_upload_quant(fg_ctx *ctx, int32_t qtype, const void *gguf_blocks, uint64_
   FG_API_BEGIN
   Guard g(ctx);
   Ctx &c = C(ctx);
-  FG_REQUIRE(is_quant(qtype), FG_ERR_DTYPE, "fg_upload_quant: qtype must be Q4_0, Q8_0 or Q4_K");
-  if (qtype == FG_Q4_K) {  // GGUF order on the device: a plain copy
+  FG_REQUIRE(is_quant(qtype), FG_ERR_DTYPE, "fg_upload_quant: qtype must be Q4_0, Q8_0, Q4_K or Q6_K");
+  if (is_kquant(qtype)) {  // GGUF order on the device: a plain copy
     FG_REQUIRE(rows >= 0 && cols >= 0 && cols % 256 == 0, FG_ERR_SHAPE,
-               "Q4_K matrix [%lld, %lld]: cols %% 256 != 0", (long long)rows, (long long)cols);
-    const uint64_t need = (uint64_t)rows * (uint64_t)(cols / 256) * 144ull;
+               "k-quant matrix [%lld, %lld]: cols %% 256 != 0", (long long)rows, (long long)cols);
+    const uint64_t need = (uint64_t)rows * (uint64_t)(cols / 256) * kquant_block_bytes(qtype);
     FG_REQUIRE(bytes == need, FG_ERR_SHAPE, "GGUF payload of %llu bytes, expected %llu", (unsigned long long)bytes,
                (unsigned long long)need);
     const int64_t shape[2] = {rows, cols};
@@ -509,7 +512,7 @@ int fg_read_quant_gguf(fg_ctx *ctx, fg_handle h, void *host, uint64_t bytes) {
   Ctx &c = C(ctx);
   Tensor &t = c.get(h);
   FG_REQUIRE(is_quant(t.dtype), FG_ERR_DTYPE, "fg_read_quant_gguf: tensor is not quantized");
-  if (t.dtype == FG_Q4_K) {
+  if (is_kquant(t.dtype)) {
     FG_REQUIRE(bytes == t.bytes, FG_ERR_SHAPE, "GGUF read of %llu bytes, expected %llu", (unsigned long long)bytes,
                (unsigned long long)t.bytes);
     if (bytes) c.d2h(host, t.ptr, bytes);
@@ -584,13 +587,17 @@ int fg_dequant(fg_ctx *ctx, fg_handle w, fg_handle *out) {
   Guard g(ctx);
   Ctx &c = C(ctx);
   Tensor &t = c.get(w);
-  FG_REQUIRE(is_quant(t.dtype), FG_ERR_DTYPE, "dequant: tensor is not Q4_0/Q8_0/Q4_K");
-  if (t.dtype == FG_Q4_K) {
+  FG_REQUIRE(is_quant(t.dtype), FG_ERR_DTYPE, "dequant: tensor is not Q4_0/Q8_0/Q4_K/Q6_K");
+  if (is_kquant(t.dtype)) {
     const int64_t shp[2] = {t.shape[0], t.shape[1]};
     const void *src = t.ptr;
+    const int dt = t.dtype;  // `t` may move when the registry grows
     Tensor *o = nullptr;
     const fg_handle h = c.make(shp, 2, FG_F32, &o);
-    launch_dequant_q4k(src, shp[0] * shp[1] / 256, (float *)o->ptr, c.stream);
+    if (dt == FG_Q4_K)
+      launch_dequant_q4k(src, shp[0] * shp[1] / 256, (float *)o->ptr, c.stream);
+    else
+      launch_dequant_q6k(src, shp[0] * shp[1] / 256, (float *)o->ptr, c.stream);
     *out = h;
     return FG_OK;
   }
@@ -607,7 +614,7 @@ namespace {
 // Validates x [..., K] against W [N, K]; returns M (rows of x).
 int64_t qmatmul_rows(const Tensor &xt, const Tensor &wt) {
   check_f32(xt, "qmatmul activations");
-  FG_REQUIRE(is_quant(wt.dtype), FG_ERR_DTYPE, "qmatmul: weight must be Q4_0/Q8_0/Q4_K");
+  FG_REQUIRE(is_quant(wt.dtype), FG_ERR_DTYPE, "qmatmul: weight must be Q4_0/Q8_0/Q4_K/Q6_K");
   const int64_t K = wt.shape[1];
   FG_REQUIRE(xt.ndim >= 1 && xt.shape[xt.ndim - 1] == K, FG_ERR_SHAPE, "qmatmul: x[..., %lld] vs W[%lld, %lld]",
              (long long)(xt.ndim ? xt.shape[xt.ndim - 1] : 0), (long long)wt.shape[0], (long long)K);
@@ -616,12 +623,15 @@ int64_t qmatmul_rows(const Tensor &xt, const Tensor &wt) {
   return M;
 }
 
-// Q4_K: GEMV for M <= 8, else the matrix dequantised into a temporary and the fp32 GEMM.
-void qmatmul_q4k(Ctx &c, const Tensor &xt, const Tensor &wt, int64_t M, float *y) {
+// Q4_K / Q6_K: GEMV for M <= 8, else the matrix dequantised into a temporary and the fp32 GEMM.
+void qmatmul_kquant(Ctx &c, const Tensor &xt, const Tensor &wt, int64_t M, float *y) {
   const int64_t N = wt.shape[0], K = wt.shape[1];
   float *scratch = nullptr;
   if (M > 8 && N * K) scratch = (float *)c.alloc(4ull * (uint64_t)(N * K));
-  launch_qmatmul_q4k(wt.ptr, N, K, (const float *)xt.ptr, M, y, scratch, c.stream);
+  if (wt.dtype == FG_Q4_K)
+    launch_qmatmul_q4k(wt.ptr, N, K, (const float *)xt.ptr, M, y, scratch, c.stream);
+  else
+    launch_qmatmul_q6k(wt.ptr, N, K, (const float *)xt.ptr, M, y, scratch, c.stream);
   if (scratch) c.free_async(scratch, 4ull * (uint64_t)(N * K));
 }
 
@@ -652,8 +662,8 @@ int fg_qmatmul(fg_ctx *ctx, fg_handle x, fg_handle w, fg_handle *out) {
   shp[xt.ndim - 1] = wt.shape[0];
   Tensor *o = nullptr;
   const fg_handle h = c.make(shp, xt.ndim, FG_F32, &o);
-  if (c.get(w).dtype == FG_Q4_K)
-    qmatmul_q4k(c, c.get(x), c.get(w), M, (float *)o->ptr);
+  if (is_kquant(c.get(w).dtype))
+    qmatmul_kquant(c, c.get(x), c.get(w), M, (float *)o->ptr);
   else
     qmatmul_launch(c, c.get(x), c.get(w).qmat(), M, (float *)o->ptr);
   *out = h;
@@ -670,8 +680,8 @@ int fg_qmatmul_into(fg_ctx *ctx, fg_handle x, fg_handle w, fg_handle out) {
   const int64_t M = qmatmul_rows(xt, wt);
   FG_REQUIRE(ot.dtype == FG_F32 && ot.numel() == M * wt.shape[0], FG_ERR_SHAPE,
              "qmatmul_into: output must be F32 [.., %lld]", (long long)wt.shape[0]);
-  if (wt.dtype == FG_Q4_K)
-    qmatmul_q4k(c, xt, wt, M, (float *)ot.ptr);
+  if (is_kquant(wt.dtype))
+    qmatmul_kquant(c, xt, wt, M, (float *)ot.ptr);
   else
     qmatmul_launch(c, xt, wt.qmat(), M, (float *)ot.ptr);
   FG_API_END

@@ -40,7 +40,7 @@ extern thread_local std::string g_last_error;
 namespace {
 
 // ggml tensor types read here
-constexpr uint32_t kGgmlF32 = 0, kGgmlF16 = 1, kGgmlQ4_0 = 2, kGgmlQ8_0 = 8, kGgmlQ4_K = 12;
+constexpr uint32_t kGgmlF32 = 0, kGgmlF16 = 1, kGgmlQ4_0 = 2, kGgmlQ8_0 = 8, kGgmlQ4_K = 12, kGgmlQ6_K = 14;
 // metadata value types
 enum : uint32_t {
   GV_U8 = 0, GV_I8 = 1, GV_U16 = 2, GV_I16 = 3, GV_U32 = 4, GV_I32 = 5, GV_F32 = 6, GV_BOOL = 7,
@@ -71,6 +71,7 @@ uint64_t type_bytes(uint32_t t, int64_t ne0, int64_t rows) {
     case kGgmlQ4_0: return ne0 % 32 ? 0 : (uint64_t)(ne0 / 32) * 18 * rows;
     case kGgmlQ8_0: return ne0 % 32 ? 0 : (uint64_t)(ne0 / 32) * 34 * rows;
     case kGgmlQ4_K: return ne0 % 256 ? 0 : (uint64_t)(ne0 / 256) * 144 * rows;
+    case kGgmlQ6_K: return ne0 % 256 ? 0 : (uint64_t)(ne0 / 256) * 210 * rows;
     default: return 0;
   }
 }
@@ -256,6 +257,7 @@ int32_t to_fg_type(uint32_t t) {
     case kGgmlQ4_0: return FG_Q4_0;
     case kGgmlQ8_0: return FG_Q8_0;
     case kGgmlQ4_K: return FG_Q4_K;
+    case kGgmlQ6_K: return FG_Q6_K;
     default: return -1;
   }
 }

@@ -437,7 +437,7 @@ fg_handle Exec::exec_node(size_t i, const void *const *inputs, const uint64_t *i
                (long long)N, (long long)B, (long long)n.numel);
     const fg_handle src = in_h(n, 0);
     Tensor &a = c.peek(src);
-    const bool quant = a.dtype == FG_Q4_0 || a.dtype == FG_Q8_0 || a.dtype == FG_Q4_K;
+    const bool quant = a.dtype == FG_Q4_0 || a.dtype == FG_Q8_0 || a.dtype == FG_Q4_K || a.dtype == FG_Q6_K;
     if (B == 1 && !a.lazy && (quant || (a.dtype == FG_F32 && consumers_only(i, {"matmul"})))) {
       FG_REQUIRE(quant ? (a.shape[0] == M && a.shape[1] == N) : a.numel() == M * N, FG_ERR_SHAPE,
                  "transpose input does not hold [%lld, %lld]", (long long)M, (long long)N);
@@ -474,7 +474,7 @@ fg_handle Exec::exec_node(size_t i, const void *const *inputs, const uint64_t *i
       Tensor &w = c.get(hw);
       FG_REQUIRE(w.shape[0] == N && w.numel() == N * K, FG_ERR_SHAPE, "%s: transposed B must come from [%lld, %lld]",
                  op.c_str(), (long long)N, (long long)K);
-      if (w.dtype == FG_Q4_0 || w.dtype == FG_Q8_0 || w.dtype == FG_Q4_K) {
+      if (w.dtype == FG_Q4_0 || w.dtype == FG_Q8_0 || w.dtype == FG_Q4_K || w.dtype == FG_Q6_K) {
         // x is [M, K]: give the activation tensor that shape for the quantized GEMV / GEMM
         FG_REQUIRE(a.ndim == 2 || M * K == 0 || a.shape[a.ndim - 1] == K, FG_ERR_SHAPE, "%s: A rows", op.c_str());
         fg_handle h = 0;
@@ -888,10 +888,12 @@ void Ctx::materialize(fg_handle h, Tensor &t) {
     const int64_t M = src.shape[0], N = src.ndim == 2 ? src.shape[1] : (M ? src.numel() / M : 0);
     const float *sp = (const float *)src.ptr;
     float *tmp = nullptr;
-    if (src.dtype == FG_Q4_0 || src.dtype == FG_Q8_0 || src.dtype == FG_Q4_K) {  // dequantise, then transpose
-      tmp = (float *)alloc(4ull * (uint64_t)src.numel());
+    if (src.dtype == FG_Q4_0 || src.dtype == FG_Q8_0 || src.dtype == FG_Q4_K || src.dtype == FG_Q6_K) {
+      tmp = (float *)alloc(4ull * (uint64_t)src.numel());  // dequantise, then transpose
       if (src.dtype == FG_Q4_K)
         launch_dequant_q4k(src.ptr, src.numel() / 256, tmp, stream);
+      else if (src.dtype == FG_Q6_K)
+        launch_dequant_q6k(src.ptr, src.numel() / 256, tmp, stream);
       else
         launch_dequant(src.qmat(), tmp, stream);
       sp = tmp;

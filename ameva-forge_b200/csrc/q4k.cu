@@ -1,4 +1,4 @@
-// GGUF Q4_K: dequantisation and the fused dequant-GEMV / GEMM.
+// GGUF k-quants (Q4_K, Q6_K): dequantisation and the fused dequant-GEMV / GEMM.
 //
 // Q4_K is the super-block format of llama.cpp's Q4_K_M files (ggml's
 // published block_q4_K; the reference's quant path stops at its 4/8-bit
@@ -17,7 +17,8 @@
 // 2(l/8) + 1, positions 4(l % 8) .. +3 -- so a warp reads the 128 nibble
 // bytes as one coalesced 128-byte line plus the 16-byte header; the scale
 // and min apply per lane before the one warp reduction at the end of the
-// row.  HBM-bound: 144 bytes per 256 weights.  Larger M dequantises the
+// row.  Eight super-blocks are loaded per pass before any is used, so each
+// warp keeps 1152 bytes in flight.  HBM-bound: 144 bytes per 256 weights.  Larger M dequantises the
 // matrix once and runs the fp32 GEMM.
 #include "runtime.cuh"
 
@@ -53,6 +54,22 @@ __global__ void k_dequant_q4k(const uint8_t *__restrict__ blocks, int64_t n_bloc
   }
 }
 
+// Byte i (0..11) of the 12 scale bytes held in the header words y, z, w (header bytes 4..15), by
+// shifts, so the header stays in registers.
+__device__ __forceinline__ int q4k_sbyte(const uint4 &h, int i) {
+  const uint64_t lo = ((uint64_t)h.z << 32) | h.y;
+  return (int)((i < 8 ? lo >> (8 * i) : (uint64_t)h.w >> (8 * (i - 8))) & 0xFF);
+}
+__device__ __forceinline__ void q4k_scale_min_r(int j, const uint4 &h, int &sc, int &m) {
+  if (j < 4) {
+    sc = q4k_sbyte(h, j) & 63;
+    m = q4k_sbyte(h, j + 4) & 63;
+  } else {
+    sc = (q4k_sbyte(h, j + 4) & 0xF) | ((q4k_sbyte(h, j - 4) >> 6) << 4);
+    m = (q4k_sbyte(h, j + 4) >> 4) | ((q4k_sbyte(h, j) >> 6) << 4);
+  }
+}
+
 constexpr int kQ4kWarps = 8;
 
 template <int M>
@@ -68,34 +85,47 @@ __global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q4k(const uint8_t *__re
   float acc[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) acc[m] = 0.0f;
-#pragma unroll 2
-  for (int64_t b = 0; b < nb; ++b) {
-    const uint8_t *blk = wr + b * 144;
-    const uint4 hdr = __ldg(reinterpret_cast<const uint4 *>(blk));  // d, dmin, scales
-    const uint32_t qw = __ldg(reinterpret_cast<const uint32_t *>(blk + 16) + lane);
-    const uint8_t *hb = reinterpret_cast<const uint8_t *>(&hdr);
-    const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
-    const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
-    int s0, m0, s1, m1;
-    q4k_scale_min(2 * c, hb + 4, s0, m0);
-    q4k_scale_min(2 * c + 1, hb + 4, s1, m1);
-    const float d0 = d * (float)s0, mm0 = dmin * (float)m0, d1 = d * (float)s1, mm1 = dmin * (float)m1;
-    float lo[4], hi[4];
+  // kU super-blocks per pass: their headers and nibble words are loaded before any is used, so a
+  // warp has kU x 144 bytes in flight
+  constexpr int kU = 8;
+  for (int64_t b0 = 0; b0 < nb; b0 += kU) {
+    uint4 hdr[kU];
+    uint32_t qw[kU];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      lo[e] = (float)((qw >> (8 * e)) & 0xF);
-      hi[e] = (float)((qw >> (8 * e + 4)) & 0xF);
+    for (int u = 0; u < kU; ++u) {
+      if (b0 + u < nb) {
+        const uint8_t *blk = wr + (b0 + u) * 144;
+        hdr[u] = __ldg(reinterpret_cast<const uint4 *>(blk));  // d, dmin, scales
+        qw[u] = __ldg(reinterpret_cast<const uint32_t *>(blk + 16) + lane);
+      }
     }
 #pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const float *xb = x + m * ldx + b * 256 + 64 * c + p;
-      const float4 xa = __ldg(reinterpret_cast<const float4 *>(xb));
-      const float4 xc = __ldg(reinterpret_cast<const float4 *>(xb + 32));
-      const float qa = lo[0] * xa.x + lo[1] * xa.y + lo[2] * xa.z + lo[3] * xa.w;
-      const float sa = xa.x + xa.y + xa.z + xa.w;
-      const float qc = hi[0] * xc.x + hi[1] * xc.y + hi[2] * xc.z + hi[3] * xc.w;
-      const float sc = xc.x + xc.y + xc.z + xc.w;
-      acc[m] += (d0 * qa - mm0 * sa) + (d1 * qc - mm1 * sc);
+    for (int u = 0; u < kU; ++u) {
+      if (b0 + u >= nb) break;
+      const int64_t b = b0 + u;
+      const float d = __half2float(__ushort_as_half((unsigned short)(hdr[u].x & 0xFFFF)));
+      const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[u].x >> 16)));
+      int s0, m0, s1, m1;
+      q4k_scale_min_r(2 * c, hdr[u], s0, m0);
+      q4k_scale_min_r(2 * c + 1, hdr[u], s1, m1);
+      const float d0 = d * (float)s0, mm0 = dmin * (float)m0, d1 = d * (float)s1, mm1 = dmin * (float)m1;
+      float lo[4], hi[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        lo[e] = (float)((qw[u] >> (8 * e)) & 0xF);
+        hi[e] = (float)((qw[u] >> (8 * e + 4)) & 0xF);
+      }
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const float *xb = x + m * ldx + b * 256 + 64 * c + p;
+        const float4 xa = __ldg(reinterpret_cast<const float4 *>(xb));
+        const float4 xc = __ldg(reinterpret_cast<const float4 *>(xb + 32));
+        const float qa = lo[0] * xa.x + lo[1] * xa.y + lo[2] * xa.z + lo[3] * xa.w;
+        const float sa = xa.x + xa.y + xa.z + xa.w;
+        const float qc = hi[0] * xc.x + hi[1] * xc.y + hi[2] * xc.z + hi[3] * xc.w;
+        const float sc = xc.x + xc.y + xc.z + xc.w;
+        acc[m] += (d0 * qa - mm0 * sa) + (d1 * qc - mm1 * sc);
+      }
     }
   }
 #pragma unroll
@@ -111,7 +141,142 @@ void gemv_q4k_launch(const uint8_t *w, int64_t N, int64_t K, const float *x, flo
   FG_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------ Q6_K
+// 256 values in 210 bytes: ql[128] (low 4 bits), qh[64] (high 2 bits), int8
+// scales[16], fp16 d.  Half h uses ql[64h..], qh[32h..], scales[8h..]; value
+// l (+32, +64, +96) of a half takes the low nibble of ql[l] (low of ql[l+32],
+// high of ql[l], high of ql[l+32]) with qh[l] bits 0-1 (2-3, 4-5, 6-7) on top,
+// minus 32, times d * scales[l/16] (+2, +4, +6): two fp32 products.  Blocks
+// stay in GGUF order (2-byte aligned); the GEMV reads them with 16-bit loads.
+__device__ __forceinline__ float q6k_d(const uint8_t *blk) {
+  return __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(blk + 208))));
+}
+
+// One thread per (super-block, half, l): four values.
+__global__ void k_dequant_q6k(const uint8_t *__restrict__ blocks, int64_t n_blocks, float *__restrict__ out) {
+  const int64_t n = n_blocks * 64;
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t b = t >> 6;
+    const int h = (int)((t >> 5) & 1), l = (int)(t & 31), is = l >> 4;
+    const uint8_t *blk = blocks + b * 210;
+    const uint8_t *ql = blk + 64 * h, *qh = blk + 128 + 32 * h;
+    const int8_t *sc = reinterpret_cast<const int8_t *>(blk + 192 + 8 * h);
+    const float d = q6k_d(blk);
+    const int q1 = ((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+    const int q2 = ((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+    const int q3 = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+    const int q4 = ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+    float *o = out + b * 256 + 128 * h + l;
+    o[0] = __fmul_rn(__fmul_rn(d, (float)sc[is]), (float)q1);
+    o[32] = __fmul_rn(__fmul_rn(d, (float)sc[is + 2]), (float)q2);
+    o[64] = __fmul_rn(__fmul_rn(d, (float)sc[is + 4]), (float)q3);
+    o[96] = __fmul_rn(__fmul_rn(d, (float)sc[is + 6]), (float)q4);
+  }
+}
+
+// GEMV: one warp per weight row; lane = (half h = lane / 16, positions 2 (lane % 16) and +1 of each
+// quarter of the half), so a warp's 16-bit loads of ql and qh cover the block's 192 code bytes.
+template <int M>
+__global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q6k(const uint8_t *__restrict__ w, int64_t N, int64_t K,
+                                                             const float *__restrict__ x, int64_t ldx,
+                                                             float *__restrict__ y, int64_t ldy) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kQ4kWarps + (threadIdx.x >> 5);
+  if (row >= N) return;
+  const int64_t nb = K / 256;
+  const uint8_t *wr = w + row * nb * 210;
+  const int h = lane >> 4, lp = 2 * (lane & 15), is = lp >> 4;
+  float acc[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+  constexpr int kU = 4;  // super-blocks whose loads are issued before any is used
+  for (int64_t b0 = 0; b0 < nb; b0 += kU) {
+    uint32_t qa[kU], qb[kU], qc[kU], sw[kU];
+    float dd[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (b0 + u < nb) {
+        const uint8_t *blk = wr + (b0 + u) * 210;
+        qa[u] = __ldg(reinterpret_cast<const unsigned short *>(blk + 64 * h + lp));
+        qb[u] = __ldg(reinterpret_cast<const unsigned short *>(blk + 64 * h + 32 + lp));
+        qc[u] = __ldg(reinterpret_cast<const unsigned short *>(blk + 128 + 32 * h + lp));
+        const uint8_t *sp = blk + 192 + 8 * h + is;
+        sw[u] = (uint32_t)__ldg(sp) | ((uint32_t)__ldg(sp + 2) << 8) | ((uint32_t)__ldg(sp + 4) << 16) |
+                ((uint32_t)__ldg(sp + 6) << 24);
+        dd[u] = q6k_d(blk);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (b0 + u >= nb) break;
+      const int64_t b = b0 + u;
+      float q[4][2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int l0 = (qa[u] >> (8 * e)) & 0xFF, l1 = (qb[u] >> (8 * e)) & 0xFF, hh = (qc[u] >> (8 * e)) & 0xFF;
+        q[0][e] = (float)(((l0 & 0xF) | ((hh & 3) << 4)) - 32);
+        q[1][e] = (float)(((l1 & 0xF) | (((hh >> 2) & 3) << 4)) - 32);
+        q[2][e] = (float)(((l0 >> 4) | (((hh >> 4) & 3) << 4)) - 32);
+        q[3][e] = (float)(((l1 >> 4) | (((hh >> 6) & 3) << 4)) - 32);
+      }
+      float scf[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) scf[k] = (float)(int8_t)((sw[u] >> (8 * k)) & 0xFF);
+#pragma unroll
+      for (int m = 0; m < M; ++m) {
+        const float *xb = x + m * ldx + b * 256 + 128 * h + lp;
+        float sum = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 xv = __ldg(reinterpret_cast<const float2 *>(xb + 32 * k));
+          sum = fmaf(scf[k], q[k][0] * xv.x + q[k][1] * xv.y, sum);
+        }
+        acc[m] = fmaf(dd[u], sum, acc[m]);
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const float v = warp_sum(acc[m]);
+    if (lane == 0) y[m * ldy + row] = v;
+  }
+}
+
+template <int M>
+void gemv_q6k_launch(const uint8_t *w, int64_t N, int64_t K, const float *x, float *y, cudaStream_t s) {
+  k_gemv_q6k<M><<<(unsigned)ceil_div(N, kQ4kWarps), kQ4kWarps * 32, 0, s>>>(w, N, K, x, K, y, N);
+  FG_LAUNCH_CHECK();
+}
+
 }  // namespace
+
+void launch_dequant_q6k(const void *blocks, int64_t n_blocks, float *out, cudaStream_t s) {
+  if (n_blocks == 0) return;
+  const int64_t n = n_blocks * 64;
+  k_dequant_q6k<<<(unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 32), 256, 0, s>>>((const uint8_t *)blocks,
+                                                                                        n_blocks, out);
+  FG_LAUNCH_CHECK();
+}
+
+// y[M, N] = x[M, K] W^T, W Q6_K [N, K]; `scratch` (N K floats) is used when M > 8.
+void launch_qmatmul_q6k(const void *w, int64_t N, int64_t K, const float *x, int64_t M, float *y, float *scratch,
+                        cudaStream_t s) {
+  if (M == 0 || N == 0) return;
+  const uint8_t *wb = (const uint8_t *)w;
+  switch (M) {
+    case 1: return gemv_q6k_launch<1>(wb, N, K, x, y, s);
+    case 2: return gemv_q6k_launch<2>(wb, N, K, x, y, s);
+    case 3: return gemv_q6k_launch<3>(wb, N, K, x, y, s);
+    case 4: return gemv_q6k_launch<4>(wb, N, K, x, y, s);
+    case 5: return gemv_q6k_launch<5>(wb, N, K, x, y, s);
+    case 6: return gemv_q6k_launch<6>(wb, N, K, x, y, s);
+    case 7: return gemv_q6k_launch<7>(wb, N, K, x, y, s);
+    case 8: return gemv_q6k_launch<8>(wb, N, K, x, y, s);
+    default:
+      launch_dequant_q6k(w, N * K / 256, scratch, s);
+      launch_matmul_f32(x, scratch, y, M, K, N, s, /*b_trans=*/true);
+  }
+}
 
 void launch_dequant_q4k(const void *blocks, int64_t n_blocks, float *out, cudaStream_t s) {
   if (n_blocks == 0) return;

@@ -15,7 +15,7 @@ _HERE = os.path.dirname(os.path.abspath(__file__))
 # experiments); by default the in-tree build is used.
 LIB_PATH = os.environ.get("FORGE_B200_LIBRARY") or os.path.join(_HERE, "_lib", "libforge_b200.so")
 
-FG_F32, FG_F16, FG_I32, FG_U8, FG_U32, FG_Q4_0, FG_Q8_0, FG_Q4_K = 0, 1, 3, 4, 5, 16, 17, 18
+FG_F32, FG_F16, FG_I32, FG_U8, FG_U32, FG_Q4_0, FG_Q8_0, FG_Q4_K, FG_Q6_K = 0, 1, 3, 4, 5, 16, 17, 18, 19
 MAX_DIMS = 8
 
 c_i32, c_i64, c_u64, c_f32 = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint64, ctypes.c_float

@@ -10,7 +10,7 @@ import numpy as np
 
 from . import _capi as C
 
-_FG_TO_NAME = {0: "F32", 1: "F16", 16: "Q4_0", 17: "Q8_0", 18: "Q4_K", -1: "unsupported"}
+_FG_TO_NAME = {0: "F32", 1: "F16", 16: "Q4_0", 17: "Q8_0", 18: "Q4_K", 19: "Q6_K", -1: "unsupported"}
 
 
 class GGUFFile:

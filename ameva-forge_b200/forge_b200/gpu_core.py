@@ -18,10 +18,10 @@ from .errors import AMEVAForgeDisposedError, AMEVAForgeDTypeError
 _NP_TO_FG = {np.dtype(np.float32): C.FG_F32, np.dtype(np.float16): C.FG_F16, np.dtype(np.int32): C.FG_I32,
              np.dtype(np.uint32): C.FG_U32, np.dtype(np.uint8): C.FG_U8}
 _FG_TO_NP = {C.FG_F32: np.float32, C.FG_F16: np.float16, C.FG_I32: np.int32, C.FG_U32: np.uint32, C.FG_U8: np.uint8}
-QTYPES = {"Q4_0": C.FG_Q4_0, "Q8_0": C.FG_Q8_0, "Q4_K": C.FG_Q4_K, C.FG_Q4_0: C.FG_Q4_0, C.FG_Q8_0: C.FG_Q8_0,
-          C.FG_Q4_K: C.FG_Q4_K}
-GGUF_BLOCK_BYTES = {C.FG_Q4_0: 18, C.FG_Q8_0: 34, C.FG_Q4_K: 144}
-GGUF_BLOCK_VALUES = {C.FG_Q4_0: 32, C.FG_Q8_0: 32, C.FG_Q4_K: 256}
+QTYPES = {"Q4_0": C.FG_Q4_0, "Q8_0": C.FG_Q8_0, "Q4_K": C.FG_Q4_K, "Q6_K": C.FG_Q6_K, C.FG_Q4_0: C.FG_Q4_0,
+          C.FG_Q8_0: C.FG_Q8_0, C.FG_Q4_K: C.FG_Q4_K, C.FG_Q6_K: C.FG_Q6_K}
+GGUF_BLOCK_BYTES = {C.FG_Q4_0: 18, C.FG_Q8_0: 34, C.FG_Q4_K: 144, C.FG_Q6_K: 210}
+GGUF_BLOCK_VALUES = {C.FG_Q4_0: 32, C.FG_Q8_0: 32, C.FG_Q4_K: 256, C.FG_Q6_K: 256}
 
 
 def _h(handle: str) -> int:

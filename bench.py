@@ -244,8 +244,9 @@ def gemv_roofline(ctx, world, reps=8, rounds=10):
 
 def gemm_table(ctx, reps=8, rounds=10):
     """Dequant-GEMV/GEMM rows of the scope table: Q4_0 W [N, K] in {4096 x
-    11008, 11008 x 4096} at batch 1/8/32/128 and the Q8_0 4096 x 4096 GEMV at
-    batch 1; W from N(0, 0.02), x ~ N(0, 1).  Cold L2: every replay rotates
+    11008, 11008 x 4096} at batch 1/8/32/128, the Q8_0 4096 x 4096 GEMV at
+    batch 1 and Q4_K / Q6_K GEMVs; W from N(0, 0.02) (k-quants: random super-blocks),
+    x ~ N(0, 1).  Cold L2: every replay rotates
     over `reps` weight copies (more than L2 together).  Graph-captured
     launches on the library stream, CUDA-event timed."""
     stream = torch.cuda.ExternalStream(ctx.stream_ptr())
@@ -254,8 +255,22 @@ def gemm_table(ctx, reps=8, rounds=10):
         peak_tf = float(json.load(f).get("bf16_tflops", 1590.0))
     rows = []
     for (qt, N, K, batches) in [("Q4_0", 4096, 11008, (1, 8, 32, 128)), ("Q4_0", 11008, 4096, (1, 8, 32, 128)),
-                                ("Q8_0", 4096, 4096, (1,))]:
-        ws = [ctx.synth_quant(qt, N, K, seed=77 + r, std=0.02) for r in range(reps)]
+                                ("Q8_0", 4096, 4096, (1,)), ("Q4_K", 4096, 11008, (1, 4)), ("Q4_K", 11008, 4096, (1,)),
+                                ("Q6_K", 4096, 11008, (1,)), ("Q6_K", 11008, 4096, (1,))]:
+        if qt in ("Q4_K", "Q6_K"):  # random super-blocks with finite fp16 scales
+            ws = []
+            bb = 144 if qt == "Q4_K" else 210
+            for r in range(reps):
+                rng = np.random.default_rng(77 + r)
+                b = rng.integers(0, 256, size=(N * K // 256, bb), dtype=np.uint8)
+                dd = (rng.random(N * K // 256) * 1e-3 + 1e-4).astype(np.float16).view(np.uint8).reshape(-1, 2)
+                if qt == "Q4_K":
+                    b[:, 0:2], b[:, 2:4] = dd, dd
+                else:
+                    b[:, 208:210] = dd
+                ws.append(ctx.upload_quant(qt, b, N, K))
+        else:
+            ws = [ctx.synth_quant(qt, N, K, seed=77 + r, std=0.02) for r in range(reps)]
         for M in batches:
             x = ctx.synth_normal((M, K), np.float32, seed=K + M)
             out = ctx.empty((M, N), np.float32)
@@ -275,9 +290,14 @@ def gemm_table(ctx, reps=8, rounds=10):
                 e1.record()
             e1.synchronize()
             us = 1000 * e0.elapsed_time(e1) / (rounds * reps)
-            byt = N * (K // 32) * (18 if qt == "Q4_0" else 34) + 4 * M * (K + N)
+            kq = {"Q4_K": 144, "Q6_K": 210}
+            byt = (N * (K // 256) * kq[qt] if qt in kq else N * (K // 32) * (18 if qt == "Q4_0" else 34)) + \
+                4 * M * (K + N)
             fl = 2.0 * M * N * K
-            kern = "k_qgemv" if M <= 4 else ("k_qgemm_tc (tcgen05)" if qt == "Q4_0" else "k_qgemm_simt")
+            if qt in kq:
+                kern = ("k_gemv_" + qt.lower().replace("_", "")) if M <= 8 else "dequant + k_matmul_f32"
+            else:
+                kern = "k_qgemv" if M <= 4 else ("k_qgemm_tc (tcgen05)" if qt == "Q4_0" else "k_qgemm_simt")
             rows.append({"qtype": qt, "N": N, "K": K, "batch": M, "kernel": kern,
                          "us": us, "GBps": byt / us / 1e3, "TFLOPs": fl / us / 1e6,
                          "hbm_frac": byt / us / 1e3 / peak_bw, "tensor_frac": fl / us / 1e6 / peak_tf})

@@ -65,9 +65,10 @@ enum {
   FG_U32 = 5,
   FG_Q4_0 = 16,
   FG_Q8_0 = 17,
-  FG_Q4_K = 18 /* GGUF Q4_K super-blocks (256 values, 144 bytes), kept in GGUF order;
-                  cols % 256 == 0.  fg_upload_quant / fg_read_quant_gguf / fg_dequant /
-                  fg_qmatmul take it (GEMV for up to 8 rows of x, else dequant + GEMM). */
+  FG_Q4_K = 18, /* GGUF k-quant super-blocks (256 values: Q4_K 144 bytes, Q6_K 210 bytes),   */
+  FG_Q6_K = 19  /* kept in GGUF order; cols % 256 == 0.  fg_upload_quant / fg_read_quant_gguf /
+                   fg_dequant / fg_qmatmul take them (GEMV for up to 8 rows of x, else dequant +
+                   GEMM); the graph front-end's transpose -> matmul fold too. */
 };
 
 typedef struct fg_ctx fg_ctx;

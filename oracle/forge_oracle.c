@@ -353,6 +353,62 @@ FO_EXPORT void fo_qmatmul_q4k(const uint8_t *blocks, int64_t N, int64_t K, const
   }
 }
 
+/*
+ * GGUF Q6_K super-block (the published ggml block_q6_K layout, the other
+ * k-quant of llama.cpp's Q4_K_M files): 256 values, 210 bytes = ql[128]
+ * (low 4 bits), qh[64] (high 2 bits), int8 scales[16], fp16 d.  Half h of the
+ * block (values 128h..128h+127) uses ql[64h..], qh[32h..], scales[8h..]; for
+ * l < 32, values l, l+32, l+64, l+96 of the half take the low nibble of
+ * ql[l], the low nibble of ql[l+32], the high nibble of ql[l], the high
+ * nibble of ql[l+32], each with 2 bits of qh[l] (bits 0-1, 2-3, 4-5, 6-7) on
+ * top, minus 32, and scales[l/16], [l/16+2], [l/16+4], [l/16+6].
+ * value = (d * scale) * q: two fp32 products.
+ */
+static inline void fo_dequant_q6k_block(const uint8_t *blk, float *out) {
+  const uint8_t *ql = blk, *qh = blk + 128;
+  const int8_t *sc = (const int8_t *)(blk + 192);
+  const float d = fo_f16_to_f32((uint16_t)(blk[208] | (blk[209] << 8)));
+  for (int h = 0; h < 2; ++h) {
+    for (int l = 0; l < 32; ++l) {
+      const int is = l / 16;
+      const int q1 = ((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+      const int q2 = ((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+      const int q3 = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+      const int q4 = ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+      out[128 * h + l] = d * (float)sc[is] * (float)q1;
+      out[128 * h + l + 32] = d * (float)sc[is + 2] * (float)q2;
+      out[128 * h + l + 64] = d * (float)sc[is + 4] * (float)q3;
+      out[128 * h + l + 96] = d * (float)sc[is + 6] * (float)q4;
+    }
+    ql += 64;
+    qh += 32;
+    sc += 8;
+  }
+}
+
+FO_EXPORT void fo_dequant_q6k(const uint8_t *blocks, int64_t n_blocks, float *out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t b = 0; b < n_blocks; ++b) fo_dequant_q6k_block(blocks + 210 * b, out + 256 * b);
+}
+
+/* y[m, n] = sum_k x[m, k] W[n, k], W Q6_K [N, K] dequantised as above; double accumulation. */
+FO_EXPORT void fo_qmatmul_q6k(const uint8_t *blocks, int64_t N, int64_t K, const float *x, int64_t M, float *y) {
+  const int64_t nb = K / 256;
+#pragma omp parallel for schedule(dynamic, 16)
+  for (int64_t n = 0; n < N; ++n) {
+    float wrow[256];
+    for (int64_t m = 0; m < M; ++m) {
+      double acc = 0.0;
+      for (int64_t b = 0; b < nb; ++b) {
+        fo_dequant_q6k_block(blocks + (n * nb + b) * 210, wrow);
+        const float *xr = x + m * K + 256 * b;
+        for (int j = 0; j < 256; ++j) acc += (double)xr[j] * (double)wrow[j];
+      }
+      y[m * N + n] = (float)acc;
+    }
+  }
+}
+
 /* Dense fp32 matmul C[M,N] = A[M,K] B[K,N]: cpuMatMul of
  * packages/forge/tests/matmul_tiled.test.ts:20 (double accumulation). */
 FO_EXPORT void fo_matmul(const float *A, const float *B, int64_t M, int64_t K, int64_t N, float *C) {

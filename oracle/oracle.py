@@ -62,6 +62,8 @@ def lib():
         L.fo_qmatmul.argtypes = [ctypes.c_int, _u8p, _i64, _i64, _f32p, _i64, _f32p]
         L.fo_dequant_q4k.argtypes = [_u8p, _i64, _f32p]
         L.fo_qmatmul_q4k.argtypes = [_u8p, _i64, _i64, _f32p, _i64, _f32p]
+        L.fo_dequant_q6k.argtypes = [_u8p, _i64, _f32p]
+        L.fo_qmatmul_q6k.argtypes = [_u8p, _i64, _i64, _f32p, _i64, _f32p]
         L.fo_matmul.argtypes = [_f32p, _f32p, _i64, _i64, _i64, _f32p]
         L.fo_attention.argtypes = [_f32p, _f32p, _f32p, _f32p, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                    ctypes.c_float, ctypes.c_int]
@@ -180,6 +182,33 @@ def random_q4k(rows: int, cols: int, seed: int, d_scale: float = 1e-3) -> np.nda
     b[:, 0], b[:, 1] = d & 0xFF, d >> 8
     b[:, 2], b[:, 3] = dm & 0xFF, dm >> 8
     return b.reshape(rows, cols // 256 * 144)
+
+
+def dequant_q6k(blocks: np.ndarray, rows: int, cols: int) -> np.ndarray:
+    """GGUF Q6_K super-blocks [rows, cols / 256 * 210] -> fp32 [rows, cols] (forge_oracle.c)."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8)
+    out = np.empty((rows, cols), dtype=np.float32)
+    lib().fo_dequant_q6k(_p(blocks.reshape(-1), _u8p), rows * cols // 256, _p(out, _f32p))
+    return out
+
+
+def qmatmul_q6k(blocks: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    M = x.size // K
+    y = np.empty((M, N), dtype=np.float32)
+    lib().fo_qmatmul_q6k(_p(np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1), _u8p), N, K,
+                         _p(x.reshape(-1), _f32p), M, _p(y, _f32p))
+    return y.reshape(x.shape[:-1] + (N,))
+
+
+def random_q6k(rows: int, cols: int, seed: int, d_scale: float = 1e-3) -> np.ndarray:
+    """Random valid Q6_K blocks: random ql / qh / int8 scales, finite positive fp16 d."""
+    rng = np.random.default_rng(seed)
+    nb = rows * cols // 256
+    b = rng.integers(0, 256, size=(nb, 210), dtype=np.uint8)
+    d = (rng.random(nb) * d_scale + d_scale / 8).astype(np.float16).view(np.uint16)
+    b[:, 208], b[:, 209] = d & 0xFF, d >> 8
+    return b.reshape(rows, cols // 256 * 210)
 
 
 def qmatmul(qtype: int, blocks: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:

@@ -87,3 +87,56 @@ def test_q4k_graph_linear(ctx):
     assert max_rel_err(ctx.read(out[str(y)]), O.qmatmul_q4k(blocks, N, K, x)) <= 1e-3
     assert np.array_equal(ctx.read(out[str(t)]), O.dequant_q4k(blocks, N, K).T)
     ctx.dispose_batch([out[str(ix)], out[str(t)], out[str(y)], h])
+
+
+# ---------------------------------------------------------------- Q6_K
+def test_q6k_known_answers():
+    b = np.zeros(210, np.uint8)
+    b[0:128] = 0x21      # ql: low nibble 1, high nibble 2
+    b[128:192] = 0xE4    # qh: bits 0-1 = 0, 2-3 = 1, 4-5 = 2, 6-7 = 3
+    sc = np.array([1, -2, 3, -4, 5, -6, 7, -8, 9, -10, 11, -12, 13, -14, 15, -16], np.int8)
+    b[192:208] = sc.view(np.uint8)
+    dh = np.float16(0.5).view(np.uint16)
+    b[208], b[209] = dh & 255, dh >> 8
+    w = O.dequant_q6k(b.reshape(1, 210), 1, 256)[0]
+    q = [-31, -15, 2, 18]  # (1 | 0 << 4), (1 | 1 << 4), (2 | 2 << 4), (2 | 3 << 4), each minus 32
+    for h in range(2):
+        for quarter in range(4):
+            for l in (0, 15, 16, 31):
+                want = np.float32(np.float32(0.5) * np.float32(sc[8 * h + l // 16 + 2 * quarter])) * np.float32(q[quarter])
+                assert w[128 * h + 32 * quarter + l] == want, (h, quarter, l)
+
+
+def test_gguf_lists_q6k_tensors(tmp_path):
+    import forge_b200
+    import gguf_write as GW
+    blocks = O.random_q6k(3, 512, 4)
+    path = os.path.join(tmp_path, "q6k.gguf")
+    GW.write(path, [("general.architecture", GW.V_STR, "llama")], [("output.weight", 14, [512, 3], blocks)])
+    with forge_b200.GGUFFile(path) as g:
+        t = {t["name"]: t for t in g.tensors()}["output.weight"]
+        assert t["dtype"] == "Q6_K" and t["dims"] == (512, 3)
+        assert np.array_equal(t["bytes"], blocks.reshape(-1))
+
+
+@pytest.mark.gpu
+def test_q6k_upload_roundtrip_and_exact_dequant(ctx):
+    blocks = O.random_q6k(96, 1024, 15)
+    h = ctx.upload_quant("Q6_K", blocks, 96, 1024)
+    assert np.array_equal(ctx.read_quant_gguf(h), blocks)
+    d = ctx.dequant(h)
+    assert np.array_equal(ctx.read(d).view(np.uint32), O.dequant_q6k(blocks, 96, 1024).view(np.uint32))
+    ctx.dispose_batch([h, d])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M", [1, 3, 8, 12])
+def test_q6k_qmatmul(ctx, M):
+    N, K = 200, 2048
+    blocks = O.random_q6k(N, K, 17 + M)
+    x = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
+    h = ctx.upload_quant("Q6_K", blocks, N, K)
+    xh = ctx.upload(x)
+    y = ctx.qmatmul(xh, h)
+    assert max_rel_err(ctx.read(y), O.qmatmul_q6k(blocks, N, K, x)) <= 1e-3
+    ctx.dispose_batch([h, xh, y])
