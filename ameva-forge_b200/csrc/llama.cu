@@ -308,8 +308,8 @@ void setup_step(fg_llama *m) {
   A.attn_part = (float *)m->dalloc((uint64_t)m->Hkv_l * smax * G * (d + 2) * 4);
   A.attn_cnt = (int *)m->dalloc((uint64_t)m->Hkv_l * 4);
   FG_CUDA(cudaMemsetAsync(A.attn_cnt, 0, (uint64_t)m->Hkv_l * 4, c.stream));
-  A.bar = (unsigned long long *)m->dalloc(16);
-  FG_CUDA(cudaMemsetAsync(A.bar, 0, 16, c.stream));
+  A.bar = (unsigned long long *)m->dalloc(kStepBarBytes);
+  FG_CUDA(cudaMemsetAsync(A.bar, 0, kStepBarBytes, c.stream));
   A.argkey = (unsigned long long *)m->dalloc(8);
   FG_CUDA(cudaMemsetAsync(A.argkey, 0, 8, c.stream));
   A.layers = dl;
@@ -618,7 +618,7 @@ int fg_llama_reset(fg_llama *m) {
   FG_CUDA(cudaMemsetAsync(m->pos, 0, (uint64_t)m->max_batch * 4, m->ctx->stream));
   if (m->use_step) {  // the step kernel's barrier, argmax and merge counters start over too
     const StepArgs &A = m->step_args;
-    FG_CUDA(cudaMemsetAsync(A.bar, 0, 16, m->ctx->stream));
+    FG_CUDA(cudaMemsetAsync(A.bar, 0, kStepBarBytes, m->ctx->stream));
     FG_CUDA(cudaMemsetAsync(A.argkey, 0, 8, m->ctx->stream));
     FG_CUDA(cudaMemsetAsync(A.attn_cnt, 0, (uint64_t)A.Hkv * 4, m->ctx->stream));
   }

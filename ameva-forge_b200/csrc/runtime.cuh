@@ -255,6 +255,8 @@ struct StepArgs {
   int vocab_l = 0, vbase = 0;         // logits of this rank: vocab_l rows from global index vbase
   float *h2 = nullptr;                // the residual's second buffer (tensor parallelism: h alternates)
 };
+// Bytes of the step kernel's grid-barrier words (zeroed at setup and reset).
+constexpr uint64_t kStepBarBytes = 2048;
 bool decode_step_supported(int d, int G, int qtype, int64_t H, int64_t I, int64_t qdim);
 size_t decode_step_xarea(int d, int G, int64_t H, int64_t I, int64_t qdim);
 size_t decode_step_smem(int d, int G, int64_t H, int64_t I, int64_t qdim);
