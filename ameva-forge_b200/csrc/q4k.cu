@@ -17,10 +17,12 @@
 // 2(l/8) + 1, positions 4(l % 8) .. +3 -- so a warp reads the 128 nibble
 // bytes as one coalesced 128-byte line plus the 16-byte header; the scale
 // and min apply per lane before the one warp reduction at the end of the
-// row.  Eight super-blocks are loaded per pass before any is used, so each
-// warp keeps 1152 bytes in flight.  HBM-bound: 144 bytes per 256 weights.  Larger M dequantises the
+// row.  Each warp streams its row through a 4-stage shared-memory ring of 8
+// super-blocks per stage (16-byte cp.async copies), so ~3.4 KB per warp are
+// in flight without holding registers.  HBM-bound: 144 bytes per 256 weights.  Larger M dequantises the
 // matrix once and runs the fp32 GEMM.
 #include "runtime.cuh"
+#include "tma.cuh"
 
 namespace fg {
 namespace {
@@ -72,48 +74,71 @@ __device__ __forceinline__ void q4k_scale_min_r(int j, const uint4 &h, int &sc, 
 
 constexpr int kQ4kWarps = 8;
 
+// Per-warp shared-memory ring of the Q4_K GEMV: kQ4kStages stages of kQ4kU super-blocks, filled with
+// 16-byte cp.async copies (no registers held for bytes in flight).
+constexpr int kQ4kU = 8, kQ4kStages = 4;
+constexpr int kQ4kStageBytes = kQ4kU * 144;                              // 1152
+constexpr int kQ4kSmem = kQ4kWarps * kQ4kStages * kQ4kStageBytes;        // 36 KB per block
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 template <int M>
 __global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q4k(const uint8_t *__restrict__ w, int64_t N, int64_t K,
                                                              const float *__restrict__ x, int64_t ldx,
                                                              float *__restrict__ y, int64_t ldy) {
-  const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * kQ4kWarps + (threadIdx.x >> 5);
-  if (row >= N) return;
+  extern __shared__ __align__(16) unsigned char q4k_ring[];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = (int64_t)blockIdx.x * kQ4kWarps + warp;
+  if (row >= N) return;  // warps are independent: no block barrier follows
   const int64_t nb = K / 256;
   const uint8_t *wr = w + row * nb * 144;
+  unsigned char *ring = q4k_ring + warp * kQ4kStages * kQ4kStageBytes;
   const int c = lane >> 3, p = 4 * (lane & 7);
+  // stage s <- super-blocks [b0, b0 + kQ4kU) of the row: 9 chunks of 16 bytes each
+  const auto issue = [&](int st, int64_t b0) {
+    const int chunks = (int)(nb - b0 < kQ4kU ? nb - b0 : kQ4kU) * 9;
+    for (int ch = lane; ch < chunks; ch += 32)
+      cp_async16(ring + st * kQ4kStageBytes + ch * 16, wr + b0 * 144 + ch * 16);
+  };
   float acc[M];
 #pragma unroll
   for (int m = 0; m < M; ++m) acc[m] = 0.0f;
-  // kU super-blocks per pass: their headers and nibble words are loaded before any is used, so a
-  // warp has kU x 144 bytes in flight
-  constexpr int kU = 8;
-  for (int64_t b0 = 0; b0 < nb; b0 += kU) {
-    uint4 hdr[kU];
-    uint32_t qw[kU];
 #pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      if (b0 + u < nb) {
-        const uint8_t *blk = wr + (b0 + u) * 144;
-        hdr[u] = __ldg(reinterpret_cast<const uint4 *>(blk));  // d, dmin, scales
-        qw[u] = __ldg(reinterpret_cast<const uint32_t *>(blk + 16) + lane);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      if (b0 + u >= nb) break;
+  for (int st = 0; st < kQ4kStages - 1; ++st) {
+    if ((int64_t)st * kQ4kU < nb) issue(st, (int64_t)st * kQ4kU);
+    cp_async_commit();
+  }
+  int it = 0;
+  for (int64_t b0 = 0; b0 < nb; b0 += kQ4kU, ++it) {
+    const int64_t bn = b0 + (int64_t)(kQ4kStages - 1) * kQ4kU;
+    if (bn < nb) issue((it + kQ4kStages - 1) % kQ4kStages, bn);
+    cp_async_commit();
+    cp_async_wait<kQ4kStages - 1>();  // this thread's copies of stage `it` have landed
+    __syncwarp();                      // ... and every lane's
+    const unsigned char *stg = ring + (it % kQ4kStages) * kQ4kStageBytes;
+    const int nu = (int)(nb - b0 < kQ4kU ? nb - b0 : kQ4kU);
+    for (int u = 0; u < nu; ++u) {
       const int64_t b = b0 + u;
-      const float d = __half2float(__ushort_as_half((unsigned short)(hdr[u].x & 0xFFFF)));
-      const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr[u].x >> 16)));
+      const uint4 hdr = *reinterpret_cast<const uint4 *>(stg + u * 144);
+      const uint32_t qw = reinterpret_cast<const uint32_t *>(stg + u * 144 + 16)[lane];
+      const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
+      const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
       int s0, m0, s1, m1;
-      q4k_scale_min_r(2 * c, hdr[u], s0, m0);
-      q4k_scale_min_r(2 * c + 1, hdr[u], s1, m1);
+      q4k_scale_min_r(2 * c, hdr, s0, m0);
+      q4k_scale_min_r(2 * c + 1, hdr, s1, m1);
       const float d0 = d * (float)s0, mm0 = dmin * (float)m0, d1 = d * (float)s1, mm1 = dmin * (float)m1;
       float lo[4], hi[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        lo[e] = (float)((qw[u] >> (8 * e)) & 0xF);
-        hi[e] = (float)((qw[u] >> (8 * e + 4)) & 0xF);
+        lo[e] = (float)((qw >> (8 * e)) & 0xF);
+        hi[e] = (float)((qw >> (8 * e + 4)) & 0xF);
       }
 #pragma unroll
       for (int m = 0; m < M; ++m) {
@@ -127,7 +152,9 @@ __global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q4k(const uint8_t *__re
         acc[m] += (d0 * qa - mm0 * sa) + (d1 * qc - mm1 * sc);
       }
     }
+    __syncwarp();  // every lane is done with this stage before a later issue refills it
   }
+  cp_async_wait<0>();
 #pragma unroll
   for (int m = 0; m < M; ++m) {
     const float v = warp_sum(acc[m]);
@@ -137,7 +164,7 @@ __global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q4k(const uint8_t *__re
 
 template <int M>
 void gemv_q4k_launch(const uint8_t *w, int64_t N, int64_t K, const float *x, float *y, cudaStream_t s) {
-  k_gemv_q4k<M><<<(unsigned)ceil_div(N, kQ4kWarps), kQ4kWarps * 32, 0, s>>>(w, N, K, x, K, y, N);
+  k_gemv_q4k<M><<<(unsigned)ceil_div(N, kQ4kWarps), kQ4kWarps * 32, kQ4kSmem, s>>>(w, N, K, x, K, y, N);
   FG_LAUNCH_CHECK();
 }
 
