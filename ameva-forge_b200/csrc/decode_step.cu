@@ -126,6 +126,23 @@ __device__ bool grid_sync(unsigned long long *count, unsigned long long target, 
   }
 }
 
+// grid_sync whose arrival is a system-scope release: the peer-memory stores of an exchange phase are
+// ordered before it, so the flag CTA 0 publishes after the barrier (a system-scope release) carries them.
+__device__ bool grid_sync_sys(unsigned long long *count, unsigned long long target, int *err) {
+  asm volatile("red.release.sys.global.add.u64 [%0], 1;" ::"l"(count) : "memory");
+  if (ld_acquire_u64(count) >= target) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    __nanosleep(32);
+    if (ld_acquire_u64(count) >= target) return true;
+    if (ld_volatile_int(err) != 0) return false;
+    if (global_ns() - t0 > kWaitTimeoutNs) {
+      atomicCAS(err, 0, DEVERR_GRID);
+      return false;
+    }
+  }
+}
+
 // Split of the attention phase: units = KV heads x splits, at most one unit per
 // virtual CTA; split s of a head covers tiles [s*nt/S, (s+1)*nt/S) of keys
 // [0, npos); the last split also takes key npos.
@@ -737,14 +754,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
     named_sync_id(kBarConsumers, kStepConsumers);
     const bool xphase = TP && (ph == PH_O || ph == PH_DOWN);
     // the partial sums this CTA stored into peer memory are visible system-wide before the arrival
-    if (tid == 0 && xphase) __threadfence_system();
     if (tid == 0 && !s_abort &&
-        !grid_sync(A.bar, (epoch * (unsigned long long)nphase + p + 1) * gridDim.x, A.err))
+        !(xphase ? grid_sync_sys(A.bar, (epoch * (unsigned long long)nphase + p + 1) * gridDim.x, A.err)
+                 : grid_sync(A.bar, (epoch * (unsigned long long)nphase + p + 1) * gridDim.x, A.err)))
       s_abort = 1;
     if (tid == 0 && blockIdx.x == 0 && xphase && !s_abort) {
       // every CTA of this rank has arrived: publish exchange xi to the other ranks
       const unsigned long long seq = xbase * (2 * L) + xchg_index(p, per) + 1;
-      __threadfence_system();
       for (int r = 0; r < A.tp; ++r)
         if (r != A.rank) st_release_sys_u64(xflag_words(A, r) + A.rank, seq);
     }

@@ -251,7 +251,7 @@ __device__ __forceinline__ void q4_stage_x(const Q4X<MV> &X, const float *x, int
 
 // q4_stage_x (MV = 1) of the tensor-parallel residual fold: the staged vector is h + parts[0] + ...
 // + parts[np - 1] (in that order), and its elements [s0, s1) are also stored to hout.  K = stride.
-static __device__ __noinline__ void q4_stage_x_fold(const Q4X<1> &X, const float *h, const float *parts, int np,
+static __device__ __forceinline__ void q4_stage_x_fold(const Q4X<1> &X, const float *h, const float *parts, int np,
                                              int64_t stride, float *hout, int s0, int s1, const float *gamma, int tid,
                                              int nth, float *ss_out) {
   const int lane = tid & 31, warp = tid >> 5;
