@@ -37,8 +37,8 @@ def make(ctx, shape, seed, cap, layered=False):
 
 
 @pytest.mark.parametrize("name,shape,plen", [
-    ("tinyllama_2layer", TINY2, 300),   # 10 tiles of keys: 10 splits of one tile
-    ("llama7b_1layer", L7B1, 300),      # 9 splits over 10 tiles (uneven), partial last tile
+    ("tinyllama_2layer", TINY2, 300),   # 10 tiles of keys: 5 splits of two tiles per KV head
+    ("llama7b_1layer", L7B1, 340),      # 11 tiles: 5 splits, the last of three tiles; partial last tile
     ("llama7b_1layer_short", L7B1, 5),  # one partial tile, one split
 ])
 def test_step_kernel_equals_layered_decode(ctx, name, shape, plen):
