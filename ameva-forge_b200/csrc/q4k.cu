@@ -56,19 +56,21 @@ __global__ void k_dequant_q4k(const uint8_t *__restrict__ blocks, int64_t n_bloc
   }
 }
 
-// Byte i (0..11) of the 12 scale bytes held in the header words y, z, w (header bytes 4..15), by
-// shifts, so the header stays in registers.
-__device__ __forceinline__ int q4k_sbyte(const uint4 &h, int i) {
-  const uint64_t lo = ((uint64_t)h.z << 32) | h.y;
-  return (int)((i < 8 ? lo >> (8 * i) : (uint64_t)h.w >> (8 * (i - 8))) & 0xFF);
-}
-__device__ __forceinline__ void q4k_scale_min_r(int j, const uint4 &h, int &sc, int &m) {
-  if (j < 4) {
-    sc = q4k_sbyte(h, j) & 63;
-    m = q4k_sbyte(h, j + 4) & 63;
+// (scale, min) of sub-blocks 2c and 2c+1 from the header words y, z, w (scale bytes 0-3, 4-7, 8-11),
+// packed as two bytes each (sc = sc(2c) | sc(2c+1) << 8, m likewise), by byte permutes: for c < 2 the
+// 6 low bits of bytes 2c, 2c+1 (scales) and 2c+4, 2c+5 (mins); for c >= 2 bytes 2c+4, 2c+5 give the
+// low 4 bits (scale: low nibble, min: high nibble) and the top 2 bits of bytes 2c-4, 2c-3 (scale) and
+// 2c, 2c+1 (min) go above them.  A lane's c is fixed, so the selectors are loop-invariant.
+__device__ __forceinline__ void q4k_pair(const uint4 &h, int c, uint32_t &sc, uint32_t &m) {
+  const uint32_t cc = (uint32_t)c & 1;
+  const uint32_t x = __byte_perm(h.y, h.z, (2 * cc) | ((2 * cc + 1) << 4) | ((4 + 2 * cc) << 8) | ((5 + 2 * cc) << 12));
+  if (c < 2) {
+    sc = x & 0x3F3Fu;
+    m = (x >> 16) & 0x3F3Fu;
   } else {
-    sc = (q4k_sbyte(h, j + 4) & 0xF) | ((q4k_sbyte(h, j - 4) >> 6) << 4);
-    m = (q4k_sbyte(h, j + 4) >> 4) | ((q4k_sbyte(h, j) >> 6) << 4);
+    const uint32_t y = __byte_perm(h.w, 0u, (2 * cc) | ((2 * cc + 1) << 4));
+    sc = (y & 0x0F0Fu) | ((x >> 2) & 0x3030u);
+    m = ((y >> 4) & 0x0F0Fu) | ((x >> 18) & 0x3030u);
   }
 }
 
@@ -130,9 +132,9 @@ __global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q4k(const uint8_t *__re
       const uint32_t qw = reinterpret_cast<const uint32_t *>(stg + u * 144 + 16)[lane];
       const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
       const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
-      int s0, m0, s1, m1;
-      q4k_scale_min_r(2 * c, hdr, s0, m0);
-      q4k_scale_min_r(2 * c + 1, hdr, s1, m1);
+      uint32_t scp, mp;
+      q4k_pair(hdr, c, scp, mp);
+      const int s0 = (int)(scp & 0xFF), s1 = (int)(scp >> 8), m0 = (int)(mp & 0xFF), m1 = (int)(mp >> 8);
       const float d0 = d * (float)s0, mm0 = dmin * (float)m0, d1 = d * (float)s1, mm1 = dmin * (float)m1;
       float lo[4], hi[4];
 #pragma unroll
