@@ -239,14 +239,17 @@ __global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q6k(const uint8_t *__re
     for (int u = 0; u < kU; ++u) {
       if (b0 + u >= nb) break;
       const int64_t b = b0 + u;
+      // the 6-bit codes of both positions at once, one per byte: quarter k takes the low (k = 0, 1) or
+      // high (k = 2, 3) nibbles of ql word a (k even) or b (k odd), and bits 2k, 2k+1 of each qh byte
+      // moved to bits 4, 5
+      const uint32_t v[4] = {(qa[u] & 0x0F0Fu) | ((qc[u] << 4) & 0x3030u), (qb[u] & 0x0F0Fu) | ((qc[u] << 2) & 0x3030u),
+                             ((qa[u] >> 4) & 0x0F0Fu) | (qc[u] & 0x3030u),
+                             ((qb[u] >> 4) & 0x0F0Fu) | ((qc[u] >> 2) & 0x3030u)};
       float q[4][2];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int l0 = (qa[u] >> (8 * e)) & 0xFF, l1 = (qb[u] >> (8 * e)) & 0xFF, hh = (qc[u] >> (8 * e)) & 0xFF;
-        q[0][e] = (float)(((l0 & 0xF) | ((hh & 3) << 4)) - 32);
-        q[1][e] = (float)(((l1 & 0xF) | (((hh >> 2) & 3) << 4)) - 32);
-        q[2][e] = (float)(((l0 >> 4) | (((hh >> 4) & 3) << 4)) - 32);
-        q[3][e] = (float)(((l1 >> 4) | (((hh >> 6) & 3) << 4)) - 32);
+      for (int k = 0; k < 4; ++k) {
+        q[k][0] = (float)((int)(v[k] & 0xFF) - 32);
+        q[k][1] = (float)((int)(v[k] >> 8) - 32);
       }
       float scf[4];
 #pragma unroll
