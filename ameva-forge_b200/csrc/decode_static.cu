@@ -73,6 +73,12 @@ extern "C" int fg_attention_decode_static(const float *q, const void *k_cache, c
                                           int64_t cache_capacity, int32_t n_kv, float scale, void *stream) {
   try {
     FG_REQUIRE(q && k_cache && v_cache && out, FG_ERR_VALIDATION, "attention_decode_static: null buffer");
+    // the kernel copies K/V in 16-byte chunks (cp.async) and reads q / writes out as fp32 words; a
+    // misaligned pointer would fault on the device instead of returning a status
+    FG_REQUIRE((((uintptr_t)k_cache | (uintptr_t)v_cache) & 15) == 0, FG_ERR_VALIDATION,
+               "attention_decode_static: k_cache and v_cache must be 16-byte aligned");
+    FG_REQUIRE((((uintptr_t)q | (uintptr_t)out) & 3) == 0, FG_ERR_VALIDATION,
+               "attention_decode_static: q and out must be 4-byte aligned");
     FG_REQUIRE(batch >= 1 && heads >= 1 && kv_heads >= 1, FG_ERR_SHAPE,
                "attention_decode_static: batch %d, heads %d, kv_heads %d must be >= 1", batch, heads, kv_heads);
     FG_REQUIRE(heads % kv_heads == 0, FG_ERR_SHAPE,

@@ -638,6 +638,64 @@ int fg_llama_set_position(fg_llama *m, int32_t batch, int32_t pos) {
   FG_LAPI_END
 }
 
+}  // extern "C"
+
+namespace {
+// Positions [0, len) of one layer's K (or V) cache for sequences [0, B): element (b, h, p, c) of this rank's
+// heads takes generator index ((b * Hkv_all + h0 + h) * len + p) * d + c, so every tensor-parallel rank
+// writes its slice of the same global cache.
+__global__ void k_synth_kv(uint64_t seed, int B, int Hkv_l, int Hkv_all, int h0, int len, int d, int cap,
+                           float stdv, __half *cache) {
+  const int64_t n = (int64_t)B * Hkv_l * len * d;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % d);
+    const int64_t r = i / d;
+    const int p = (int)(r % len);
+    const int64_t bh = r / len;
+    const int h = (int)(bh % Hkv_l), b = (int)(bh / Hkv_l);
+    const uint64_t gi = ((uint64_t)((int64_t)b * Hkv_all + h0 + h) * len + p) * d + c;
+    cache[(((int64_t)b * Hkv_l + h) * cap + p) * d + c] = __float2half_rn(__fadd_rn(__fmul_rn(normal01(seed, gi), stdv), 0.0f));
+  }
+}
+}  // namespace
+
+extern "C" {
+
+int fg_llama_synthesize_kv(fg_llama *m, uint64_t seed, int32_t batch, int32_t len, float stdv) {
+  FG_LAPI_BEGIN
+  LGuard g(m);
+  Ctx &c = *m->ctx;
+  FG_REQUIRE(batch >= 1 && batch <= m->max_batch, FG_ERR_SHAPE, "batch %d outside [1, %d]", batch, m->max_batch);
+  FG_REQUIRE(len >= 0 && len < m->cap, FG_ERR_SHAPE, "length %d outside [0, %d)", len, m->cap);
+  const int64_t n = (int64_t)batch * m->Hkv_l * len * m->d;
+  if (n > 0) {
+    const int grid = (int)std::min<int64_t>(ceil_div(n, 256), (int64_t)c.num_sms * 16);
+    for (int l = 0; l < (int)m->layers.size(); ++l) {
+      const LayerW &w = m->layers[l];
+      k_synth_kv<<<grid, 256, 0, c.stream>>>(tensor_seed(seed, l, 9), batch, m->Hkv_l, m->cfg.num_key_value_heads,
+                                             m->rank * m->Hkv_l, len, m->d, m->cap, stdv, w.k);
+      FG_LAUNCH_CHECK();
+      k_synth_kv<<<grid, 256, 0, c.stream>>>(tensor_seed(seed, l, 10), batch, m->Hkv_l, m->cfg.num_key_value_heads,
+                                             m->rank * m->Hkv_l, len, m->d, m->cap, stdv, w.v);
+      FG_LAUNCH_CHECK();
+    }
+  }
+  std::vector<int32_t> p((size_t)m->max_batch, 0);
+  for (int b = 0; b < batch; ++b) p[(size_t)b] = len;
+  c.h2d(m->pos, p.data(), p.size() * 4);
+  m->host_pos = len;
+  c.sync();
+  FG_LAPI_END
+}
+
+int fg_llama_decode_path(fg_llama *m, int32_t batch, int32_t *kind) {
+  FG_LAPI_BEGIN
+  FG_REQUIRE(m && kind, FG_ERR_VALIDATION, "fg_llama_decode_path: null argument");
+  FG_REQUIRE(batch >= 1 && batch <= m->max_batch, FG_ERR_SHAPE, "batch %d outside [1, %d]", batch, m->max_batch);
+  *kind = (batch == 1 && m->use_step) ? 1 : 0;
+  FG_LAPI_END
+}
+
 int fg_llama_position(fg_llama *m, int32_t *pos) {
   FG_LAPI_BEGIN
   *pos = m->host_pos;

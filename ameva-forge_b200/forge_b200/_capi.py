@@ -95,6 +95,8 @@ _SIGS = {
     "fg_llama_tokens": [c_vp, c_vp, c_i64],
     "fg_llama_get_config": [c_vp, P(LlamaConfigC)],
     "fg_llama_set_position": [c_vp, c_i32, c_i32],
+    "fg_llama_synthesize_kv": [c_vp, c_u64, c_i32, c_i32, c_f32],
+    "fg_llama_decode_path": [c_vp, c_i32, P(c_i32)],
     "fg_sample": [c_vp, c_h, ctypes.c_double, c_i32, ctypes.c_double, c_i32, ctypes.c_uint32, P(c_h)],
     "fg_gguf_open": [ctypes.c_char_p, P(c_vp)],
     "fg_gguf_close": [c_vp],

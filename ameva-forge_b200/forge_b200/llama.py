@@ -101,6 +101,19 @@ class LlamaForCausalLM:
         cache keeps its contents: zeros after creation)."""
         C.call("fg_llama_set_position", self._p, batch, pos)
 
+    def synthesize_kv(self, seed: int, length: int, batch: int = 1, std: float = 1.0):
+        """Seeded fp16 values in cache positions [0, length) of every layer for
+        sequences [0, batch), and cache length `length` (a prefilled context
+        without a prefill)."""
+        C.call("fg_llama_synthesize_kv", self._p, seed & (2**64 - 1), batch, length, std)
+
+    def decode_path(self, batch: int = 1) -> str:
+        """'step' when a decode step of `batch` sequences runs the persistent
+        one-launch kernel, 'layered' for the per-op kernels."""
+        v = ctypes.c_int32()
+        C.call("fg_llama_decode_path", self._p, batch, ctypes.byref(v))
+        return "step" if v.value == 1 else "layered"
+
     @property
     def position(self) -> int:
         v = ctypes.c_int32()

@@ -182,7 +182,10 @@ int fg_flash_attention(fg_ctx *ctx, fg_handle q, fg_handle k, fg_handle v, float
  * the device, hosts without an fg_ctx).  Raw device pointers: q and out F32
  * [batch, heads, head_dim]; k_cache and v_cache F16 [batch, kv_heads,
  * cache_capacity, head_dim], of which the first n_kv positions are attended.
- * head_dim 64 or 128, heads / kv_heads in {1, 2, 4, 8}.  Runs on `stream`
+ * head_dim 64 or 128, heads / kv_heads in {1, 2, 4, 8}.  k_cache and
+ * v_cache must be 16-byte aligned (the kernel copies 16-byte chunks of them)
+ * and q and out 4-byte aligned; other pointers give FG_ERR_VALIDATION.
+ * Runs on `stream`
  * (a cudaStream_t; NULL = legacy default stream) of the current device.
  * Split-KV scratch comes from a 2 MiB static device array: shapes that need
  * more return FG_ERR_VALIDATION.  Calls on one device must not overlap in
@@ -305,6 +308,18 @@ int fg_llama_tokens(fg_llama *m, int32_t *host, int64_t count);
  * prefill: positions [0, pos) keep whatever the cache holds (zeros after
  * creation).  For decode measurements at a given context. */
 int fg_llama_set_position(fg_llama *m, int32_t batch, int32_t pos);
+/* Fills positions [0, len) of every layer's KV cache for sequences
+ * [0, batch) with seeded fp16 values and sets their cache length to len (a
+ * context "prefilled" without running a prefill; new: the reference always
+ * prefills).  Key (b, kv head h, position p, dim c) of layer l is
+ * fp16(std * N01(splitmix64(seed, l*16 + 9), ((b*Hkv + h)*len + p)*d + c)),
+ * values use l*16 + 10; h counts the model's KV heads, so under tensor
+ * parallelism each rank writes its heads' slice of the same global cache. */
+int fg_llama_synthesize_kv(fg_llama *m, uint64_t seed, int32_t batch, int32_t len, float stdv);
+/* Which kernel runs a decode step of `batch` sequences: 1 = the persistent
+ * one-launch step kernel, 0 = the layered per-op kernels (new; for tests and
+ * tools that must know which path they measured). */
+int fg_llama_decode_path(fg_llama *m, int32_t batch, int32_t *kind);
 /* The configuration the model was created with. */
 int fg_llama_get_config(fg_llama *m, fg_llama_config *cfg);
 

@@ -451,6 +451,18 @@ class LlamaRef:
         self.pos = 0
         self.embed = f16_to_f32(w.embed_f16)
 
+    def synthesize_kv(self, seed: int, length: int, std: float = 1.0):
+        """The cache fill of fg_llama_synthesize_kv: key (b, h, p, c) of layer l
+        = fp16(std * N01(splitmix64(seed, l*16 + 9), ((b*Hkv + h)*length + p)*d + c)),
+        values with l*16 + 10; the cache length becomes `length`."""
+        s = self.s
+        n = self.batch * s.num_key_value_heads * length * s.head_dim
+        shp = (self.batch, s.num_key_value_heads, length, s.head_dim)
+        for li in range(s.num_hidden_layers):
+            self.k[li][:, :, :length] = round_f16(normal(tensor_seed(seed, li, 9), 0, n, 0.0, std).reshape(shp))
+            self.v[li][:, :, :length] = round_f16(normal(tensor_seed(seed, li, 10), 0, n, 0.0, std).reshape(shp))
+        self.pos = length
+
     def _lin(self, blocks, N, K, x):
         return qmatmul(self.w.qtype, blocks, N, K, x)
 

@@ -113,4 +113,8 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AMEVA_FORGE_REFERENCE", "")
+    if not root:
+        sys.exit(f"usage: python {os.path.basename(__file__)} <reference checkout root> "
+                 "(or set AMEVA_FORGE_REFERENCE)")
+    main(root)

@@ -5,8 +5,12 @@ and greedy tokens of the TP=1 model on the same synthesized weights.
 Each rank synthesizes only its shard; shards are slices of the same global
 tensors (counter-based generator with global row/column offsets), so the two
 runs differ only in the order of the all-reduced partial sums.  The prompt
-(40 tokens) takes the tensor-core GEMM and attention; the decode steps take
-the layered path with NCCL (TP=2) and the persistent step kernel (TP=1).
+(40 tokens) takes the tensor-core GEMM and attention with NCCL all-reduces;
+the batch-1 decode steps take the persistent step kernel on both sides: at
+TP=2 its tensor-parallel instance, which exchanges the o_proj / down_proj
+partial sums and the greedy keys over NVLink peer memory inside the kernel
+(no NCCL).  Each run records the decode path it took, and the test asserts
+it was the step kernel.
 """
 import os
 import time
@@ -27,6 +31,7 @@ def _run(ctx, out_path):
     cfg = forge_b200.LlamaConfig(max_position_embeddings=64, max_batch=1, qtype="Q4_0", **SHAPE)
     m = forge_b200.LlamaForCausalLM(cfg, ctx)
     m.synthesize(SEED)
+    path = m.decode_path(1)
     logits, nxt = m.forward(PROMPT)
     seq = [logits[0].copy()]
     toks = [int(nxt[0])]
@@ -37,7 +42,7 @@ def _run(ctx, out_path):
         toks.append(int(ids[0]))
     m.close()
     if out_path:
-        np.savez(out_path, logits=np.stack(seq), tokens=np.array(toks))
+        np.savez(out_path, logits=np.stack(seq), tokens=np.array(toks), path=np.array(path))
 
 
 def _rank(rank, world, nid, out_dir):
@@ -70,3 +75,4 @@ def test_two_gpu_tensor_parallel_matches_single_gpu(tmp_path):
     err = np.abs(a["logits"] - ref).max() / np.abs(ref).max()
     assert err <= 1e-3, err
     assert list(a["tokens"]) == list(b["tokens"])
+    assert str(a["path"]) == "step" and str(b["path"]) == "step"
