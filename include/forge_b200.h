@@ -3,7 +3,7 @@
  * AMEVA-Forge (uno-km/ameva-forge).
  *
  * The library replaces the reference's WebGPU backend (device, buffer pool,
- * staging ring, pipeline cache, quota: packages/forge/src/webgpu/*) and the
+ * staging ring, pipeline cache, quota: packages/forge/src/webgpu/) and the
  * encode/submit halves of gpuCore.dispatchKernel (packages/forge/src/tensor/
  * gpuCore.ts:500-600) and executeGraph (packages/forge/src/tensor/
  * graphExecutor.ts:517-1979).  Its op entry points mirror gpuCore's op API
