@@ -22,8 +22,10 @@
 //    run of 32-key tiles of keys [0, pos) (streamed through the ring: K tile
 //    and V tile, one bulk copy each); the unit of the last split adds key
 //    pos -- this step's K/V, written by the QKV phase -- from global memory,
-//    so the producer never waits on this step's results.  A unit's partial
-//    (max, sum, output) is merged by the last unit of its head to arrive;
+//    so the producer never waits on this step's results.  Every unit of a
+//    head publishes its partial (max, sum, output), waits for the head's
+//    other splits on a per-head counter, and merges its own slice of the
+//    head's outputs;
 //  * ARGMAX: every CTA reduces a slice of the logits to a 64-bit key (value,
 //    then lowest index; the sampler's NaN rules, sampling.ts:45-55) and
 //    atomicMax-es it; after one more barrier CTA 0 writes the token, logs it
@@ -118,6 +120,20 @@ __device__ bool grid_sync(unsigned long long *count, unsigned long long target, 
   for (;;) {
     __nanosleep(32);
     if (ld_acquire_u64(count) >= target) return true;
+    if (ld_volatile_int(err) != 0) return false;
+    if (global_ns() - t0 > kWaitTimeoutNs) {
+      atomicCAS(err, 0, DEVERR_GRID);
+      return false;
+    }
+  }
+}
+
+// Wait (bounded acquire poll) until the counter reaches `target`.
+__device__ bool wait_count(const unsigned long long *cnt, unsigned long long target, int *err) {
+  if (ld_acquire_u64(cnt) >= target) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (ld_acquire_u64(cnt) >= target) return true;
     if (ld_volatile_int(err) != 0) return false;
     if (global_ns() - t0 > kWaitTimeoutNs) {
       atomicCAS(err, 0, DEVERR_GRID);
@@ -250,6 +266,83 @@ __device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, Q
 }
 
 namespace {
+
+// The ring stages one virtual CTA's producer fills over a whole launch, in consumption order: GEMV phases
+// give the tiles of its strips (one contiguous copy each), ATTN phases the K and V rows of its unit's
+// 32-key tiles (two copies).
+template <int D>
+struct StepCursor {
+  const StepArgs *A;
+  int p, nphase, L, vk, P, npos;
+  int kind;  // 0: between phases, 1: GEMV strips, 2: attention tiles
+  const unsigned char *src;
+  int nq, u, u1, q0;
+  const __half *kc, *vc;
+  int t, t1;
+
+  __device__ void init(const StepArgs &a, int vk_, int P_, int npos_) {
+    A = &a;
+    p = -1;
+    L = a.L;
+    nphase = 5 * L + 3;
+    vk = vk_;
+    P = P_;
+    npos = npos_;
+    kind = 0;
+  }
+  // The next stage's copies: (a, ba) and, for attention, (b, bb); false after the last stage.
+  __device__ bool next(const void *&a, uint32_t &ba, const void *&b, uint32_t &bb) {
+    for (;;) {
+      if (kind == 1 && u < u1) {
+        a = src + ((int64_t)u * nq + q0) * kQ4QuadBytes;
+        ba = (uint32_t)min(kQ4TileQuads, nq - q0) * kQ4QuadBytes;
+        b = nullptr;
+        bb = 0;
+        q0 += kQ4TileQuads;
+        if (q0 >= nq) {
+          q0 = 0;
+          ++u;
+        }
+        return true;
+      }
+      if (kind == 2 && t < t1) {
+        const int nk = min(kKeysPerTile, npos - t * kKeysPerTile);
+        a = kc + (int64_t)t * kKeysPerTile * D;
+        b = vc + (int64_t)t * kKeysPerTile * D;
+        ba = bb = (uint32_t)nk * D * 2;
+        ++t;
+        return true;
+      }
+      if (++p >= nphase) return false;
+      const Phase ph = phase_kind(p, L, 5);
+      const int l = (p - 1) / 5;
+      kind = 0;
+      if (ph == PH_ATTN) {
+        const AttnSplit sp = attn_split(npos, A->Hkv, P);
+        if (vk < sp.units) {
+          const int hk = vk / sp.S, s = vk % sp.S;
+          t = s * sp.nt / sp.S;
+          t1 = (s + 1) * sp.nt / sp.S;
+          kc = A->layers[l].k + (int64_t)hk * A->cap * D;
+          vc = A->layers[l].v + (int64_t)hk * A->cap * D;
+          kind = 2;
+        }
+      } else if (ph >= PH_QKV && ph <= PH_LM) {
+        QMat w;
+        const float *x, *gm;
+        Epilogue ep;
+        gemv_phase(*A, ph, l, w, x, gm, ep);
+        const Sched sc = make_sched(w.N, kQ4StripRows, 1, vk, P);
+        src = reinterpret_cast<const unsigned char *>(w.qs);
+        nq = (int)w.row_words;
+        u = sc.u0;
+        u1 = sc.u1;
+        q0 = 0;
+        kind = 1;
+      }
+    }
+  }
+};
 
 // ---------------------------------------------------------------------------
 // Attention consumer: one unit (KV head hk, keys of tiles [t0, t1) + the
@@ -486,6 +579,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   float *reds = reinterpret_cast<float *>(xarea + A.xarea_bytes);         // [2][128]
   const int npos = A.pos[0];                                              // keys already in the cache
   const unsigned long long epoch = *reinterpret_cast<volatile unsigned long long *>(A.bar + 1);
+  // arrivals every head's attention counter received in earlier launches (each launch adds L S)
+  const unsigned long long abase = *reinterpret_cast<volatile unsigned long long *>(A.bar + 2);
   // exchange sequence base of this launch (2 L exchanges per launch; tensor parallelism only)
   const unsigned long long xbase = TP ? *reinterpret_cast<volatile unsigned long long *>(A.xep) : 0ull;
 
@@ -508,38 +603,20 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
     unsigned char *ring = rings + grp * kStepStages * kQ4TileBytes;
     uint64_t *fl = full[grp], *em = empty[grp];
     const uint64_t pol = l2_evict_first_policy();
+    StepCursor<D> ld;
+    ld.init(A, vk, P, npos);
+    const void *a, *b;
+    uint32_t ba, bb;
     int i = 0;
-    bool ok = true;
-    for (int p = 0; p < nphase && ok; ++p) {
-      const Phase ph = phase_kind(p, L, per);
-      const int l = (p - 1) / per;
-      if (ph == PH_ATTN) {
-        const AttnSplit sp = attn_split(npos, A.Hkv, P);
-        if (vk >= sp.units) continue;
-        const int hk = vk / sp.S, s = vk % sp.S;
-        const int t0 = s * sp.nt / sp.S, t1 = (s + 1) * sp.nt / sp.S;
-        const __half *kc = A.layers[l].k + (int64_t)hk * A.cap * D, *vc = A.layers[l].v + (int64_t)hk * A.cap * D;
-        for (int t = t0; t < t1 && ok; ++t, ++i) {
-          const int st = i % kStepStages;
-          if (i >= kStepStages && !mbar_wait(&em[st], (uint32_t)(i / kStepStages - 1) & 1, A.err, DEVERR_GEMV_EMPTY)) {
-            ok = false;
-            break;
-          }
-          const int nk = min(kKeysPerTile, npos - t * kKeysPerTile);
-          const uint32_t bytes = (uint32_t)nk * D * 2;
-          unsigned char *slot = ring + st * kQ4TileBytes;
-          mbar_arrive_expect_tx(&fl[st], 2 * bytes);
-          bulk_g2s(slot, kc + (int64_t)t * kKeysPerTile * D, bytes, &fl[st], pol);
-          bulk_g2s(slot + kKeysPerTile * D * 2, vc + (int64_t)t * kKeysPerTile * D, bytes, &fl[st], pol);
-        }
-      } else if (ph >= PH_QKV && ph <= PH_LM && ph != PH_ATTN) {
-        QMat w;
-        const float *x, *gm;
-        Epilogue ep;
-        gemv_phase(A, ph, l, w, x, gm, ep);
-        const Sched sc = make_sched(w.N, kQ4StripRows, 1, vk, P);
-        ok = produce_q4_strips<kStepStages>(w, sc.u0, sc.u1, ring, fl, em, i, pol, A.err);
-      }
+    while (ld.next(a, ba, b, bb)) {
+      const int st = i % kStepStages;
+      if (i >= kStepStages && !mbar_wait(&em[st], (uint32_t)(i / kStepStages - 1) & 1, A.err, DEVERR_GEMV_EMPTY))
+        break;
+      unsigned char *slot = ring + st * kQ4TileBytes;
+      mbar_arrive_expect_tx(&fl[st], ba + bb);
+      bulk_g2s(slot, a, ba, &fl[st], pol);
+      if (bb) bulk_g2s(slot + kKeysPerTile * D * 2, b, bb, &fl[st], pol);
+      ++i;
     }
     drain_ring<kStepStages>(fl, i, A.err);
     return;
@@ -635,40 +712,54 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
           }
         }
         if (sp.S > 1) {
-          __threadfence();
+          // every split of the head publishes its partial (one release add on the head's counter, which
+          // only grows: abase counts the arrivals of earlier launches), waits until all S have, and then
+          // merges its own slice [s G D / S, (s + 1) G D / S) of the head's outputs -- one round of loads
+          // instead of a lone last split walking all S partials
           named_sync_id(gbar, kGroupThreads);
-          if (gtid == 0) s_last[grp] = atomicAdd(A.attn_cnt + hk, 1) == sp.S - 1;
+          if (gtid == 0) {
+            unsigned long long *cnt = A.attn_cnt + hk;
+            asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(cnt) : "memory");
+            s_last[grp] = wait_count(cnt, abase + (unsigned long long)(l + 1) * sp.S, A.err) ? 1 : 0;
+          }
           named_sync_id(gbar, kGroupThreads);
-          if (s_last[grp]) {
-            // the last split of the head merges all S partials: warp g finds g's max and sum and writes
-            // the weights exp(m_q - M) [S][G] over the o area (S <= 8 D), then every thread sums its outputs
-            __threadfence();
-            const float *hp = A.attn_part + (int64_t)hk * sp.S * G * (D + 2);
-            float *wq = wo;
-            if (gw < G) {
-              const int g = gw;
-              float M = -INFINITY;
-              for (int q = lane; q < sp.S; q += 32) M = fmaxf(M, __ldcg(hp + (q * G + g) * (D + 2)));
-              M = warp_max(M);
-              float Ls = 0.0f;
-              for (int q = lane; q < sp.S; q += 32) {
-                const float mq = __ldcg(hp + (q * G + g) * (D + 2));
-                const float e2 = mq == -INFINITY ? 0.0f : expf(mq - M);
-                wq[q * G + g] = e2;
-                Ls = fmaf(__ldcg(hp + (q * G + g) * (D + 2) + 1), e2, Ls);
+          ok = ok && s_last[grp] != 0;
+          const float *hp = A.attn_part + (int64_t)hk * sp.S * G * (D + 2);
+          const int o0 = s * G * D / sp.S, o1 = (s + 1) * G * D / sp.S;
+          // a team of TS lanes per output (TS a power of two <= 16, >= S when S <= 16)
+          const int TS = sp.S > 8 ? 16 : (sp.S > 4 ? 8 : (sp.S > 2 ? 4 : 2));
+          const int team = gtid / TS, tl = gtid % TS, nteams = kGroupThreads / TS;
+          const int npass = (o1 - o0 + nteams - 1) / nteams;
+          for (int pass = 0; pass < npass; ++pass) {
+            const int o = o0 + pass * nteams + team;
+            const bool valid = ok && o < o1;
+            const int g = valid ? o / D : 0, c = valid ? o % D : 0;
+            float m = -INFINITY, ls = 0.0f, os = 0.0f;
+            if (valid) {
+              for (int j = tl; j < sp.S; j += TS) {
+                const float *pj = hp + (j * G + g) * (D + 2);
+                const float mj = __ldcg(pj), lj = __ldcg(pj + 1), oj = __ldcg(pj + 2 + c);
+                const float mn = fmaxf(m, mj);
+                const float f0 = m == -INFINITY ? 0.0f : expf(m - mn), f1 = mj == -INFINITY ? 0.0f : expf(mj - mn);
+                ls = ls * f0 + lj * f1;
+                os = os * f0 + oj * f1;
+                m = mn;
               }
-              Ls = warp_sum(Ls);
-              if (lane == 0) wml[g] = 1.0f / fmaxf(Ls, 1e-12f);
             }
-            named_sync_id(gbar, kGroupThreads);
-            for (int e = gtid; e < G * D; e += kGroupThreads) {
-              const int g = e / D, c = e % D;
-              float O = 0.0f;
-#pragma unroll 8
-              for (int q = 0; q < sp.S; ++q) O = fmaf(__ldcg(hp + (q * G + g) * (D + 2) + 2 + c), wq[q * G + g], O);
-              A.att[(int64_t)(hk * G + g) * D + c] = O * wml[g];
+#pragma unroll
+            for (int off = 8; off >= 1; off >>= 1) {
+              if (off < TS) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+                const float l2 = __shfl_xor_sync(0xffffffffu, ls, off);
+                const float o2 = __shfl_xor_sync(0xffffffffu, os, off);
+                const float mn = fmaxf(m, m2);
+                const float f0 = m == -INFINITY ? 0.0f : expf(m - mn), f1 = m2 == -INFINITY ? 0.0f : expf(m2 - mn);
+                ls = ls * f0 + l2 * f1;
+                os = os * f0 + o2 * f1;
+                m = mn;
+              }
             }
-            if (gtid == 0) A.attn_cnt[hk] = 0;  // ready for the next layer
+            if (valid && tl == 0) A.att[(int64_t)(hk * G + g) * D + c] = os / fmaxf(ls, 1e-12f);
           }
         }
       }
@@ -753,10 +844,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
     if (!ok) s_abort = 1;
     named_sync_id(kBarConsumers, kStepConsumers);
     const bool xphase = TP && (ph == PH_O || ph == PH_DOWN);
+    const unsigned long long btarget = (epoch * (unsigned long long)nphase + p + 1) * gridDim.x;
     // the partial sums this CTA stored into peer memory are visible system-wide before the arrival
     if (tid == 0 && !s_abort &&
-        !(xphase ? grid_sync_sys(A.bar, (epoch * (unsigned long long)nphase + p + 1) * gridDim.x, A.err)
-                 : grid_sync(A.bar, (epoch * (unsigned long long)nphase + p + 1) * gridDim.x, A.err)))
+        !(xphase ? grid_sync_sys(A.bar, btarget, A.err) : grid_sync(A.bar, btarget, A.err)))
       s_abort = 1;
     if (tid == 0 && blockIdx.x == 0 && xphase && !s_abort) {
       // every CTA of this rank has arrived: publish exchange xi to the other ranks
@@ -781,6 +872,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
     *A.step = st + 1;
     A.pos[0] = npos + 1;
     *A.argkey = 0ull;
+    const AttnSplit sp = attn_split(npos, A.Hkv, 2 * gridDim.x);
+    A.bar[2] = abase + (sp.S > 1 ? (unsigned long long)L * sp.S : 0ull);  // this launch's counter arrivals
     A.bar[1] = epoch + 1;  // every CTA has passed every barrier of this launch
   }
 }

@@ -306,8 +306,8 @@ void setup_step(fg_llama *m) {
   const int P = decode_step_vctas(c.num_sms);
   const int smax = std::max(1, P / m->Hkv_l);
   A.attn_part = (float *)m->dalloc((uint64_t)m->Hkv_l * smax * G * (d + 2) * 4);
-  A.attn_cnt = (int *)m->dalloc((uint64_t)m->Hkv_l * 4);
-  FG_CUDA(cudaMemsetAsync(A.attn_cnt, 0, (uint64_t)m->Hkv_l * 4, c.stream));
+  A.attn_cnt = (unsigned long long *)m->dalloc((uint64_t)m->Hkv_l * 8);
+  FG_CUDA(cudaMemsetAsync(A.attn_cnt, 0, (uint64_t)m->Hkv_l * 8, c.stream));
   A.bar = (unsigned long long *)m->dalloc(kStepBarBytes);
   FG_CUDA(cudaMemsetAsync(A.bar, 0, kStepBarBytes, c.stream));
   A.argkey = (unsigned long long *)m->dalloc(8);
@@ -620,7 +620,7 @@ int fg_llama_reset(fg_llama *m) {
     const StepArgs &A = m->step_args;
     FG_CUDA(cudaMemsetAsync(A.bar, 0, kStepBarBytes, m->ctx->stream));
     FG_CUDA(cudaMemsetAsync(A.argkey, 0, 8, m->ctx->stream));
-    FG_CUDA(cudaMemsetAsync(A.attn_cnt, 0, (uint64_t)A.Hkv * 4, m->ctx->stream));
+    FG_CUDA(cudaMemsetAsync(A.attn_cnt, 0, (uint64_t)A.Hkv * 8, m->ctx->stream));
   }
   m->host_pos = 0;
   FG_LAPI_END

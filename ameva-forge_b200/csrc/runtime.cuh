@@ -241,8 +241,8 @@ struct StepArgs {
   unsigned long long *argkey;  // 0 between launches
   GemvScratch gs;              // error word
   float *attn_part;            // [Hkv][2 SMs / Hkv][G][d + 2]
-  int *attn_cnt;               // [Hkv], 0 between launches
-  unsigned long long *bar;     // [2] grid barrier: arrivals, launches (never reset)
+  unsigned long long *attn_cnt;  // [Hkv] arrivals of the head's attention splits (never reset)
+  unsigned long long *bar;     // grid barrier arrivals, launches; attention arrivals per head so far (never reset)
   int *err;
   uint64_t xarea_bytes;
   // tensor parallelism (tp > 1): rank r's exchange region at xr[r] (a peer mapping for r != rank):
