@@ -623,16 +623,30 @@ int64_t qmatmul_rows(const Tensor &xt, const Tensor &wt) {
   return M;
 }
 
-// Q4_K / Q6_K: GEMV for M <= 8, else the matrix dequantised into a temporary and the fp32 GEMM.
+// Q4_K / Q6_K: GEMV for M <= 8, else the matrix dequantised (bit-exact) into a temporary and the fp32
+// matmul (the tensor-core path for all but small products).
 void qmatmul_kquant(Ctx &c, const Tensor &xt, const Tensor &wt, int64_t M, float *y) {
   const int64_t N = wt.shape[0], K = wt.shape[1];
-  float *scratch = nullptr;
-  if (M > 8 && N * K) scratch = (float *)c.alloc(4ull * (uint64_t)(N * K));
-  if (wt.dtype == FG_Q4_K)
-    launch_qmatmul_q4k(wt.ptr, N, K, (const float *)xt.ptr, M, y, scratch, c.stream);
-  else
-    launch_qmatmul_q6k(wt.ptr, N, K, (const float *)xt.ptr, M, y, scratch, c.stream);
-  if (scratch) c.free_async(scratch, 4ull * (uint64_t)(N * K));
+  if (M <= 8) {
+    if (wt.dtype == FG_Q4_K)
+      launch_qmatmul_q4k(wt.ptr, N, K, (const float *)xt.ptr, M, y, nullptr, c.stream);
+    else
+      launch_qmatmul_q6k(wt.ptr, N, K, (const float *)xt.ptr, M, y, nullptr, c.stream);
+    return;
+  }
+  if (N * K == 0) return;
+  float *w32 = (float *)c.alloc(4ull * (uint64_t)(N * K));
+  try {
+    if (wt.dtype == FG_Q4_K)
+      launch_dequant_q4k(wt.ptr, N * K / 256, w32, c.stream);
+    else
+      launch_dequant_q6k(wt.ptr, N * K / 256, w32, c.stream);
+    launch_matmul(c, (const float *)xt.ptr, w32, y, M, K, N, /*b_trans=*/true);
+  } catch (...) {
+    c.free_async(w32, 4ull * (uint64_t)(N * K));
+    throw;
+  }
+  c.free_async(w32, 4ull * (uint64_t)(N * K));
 }
 
 void qmatmul_launch(Ctx &c, const Tensor &xt, const QMat &q, int64_t M, float *y) {
@@ -700,8 +714,8 @@ int fg_matmul(fg_ctx *ctx, fg_handle a, fg_handle b, fg_handle *out) {
   const int64_t shp[2] = {at.shape[0], bt.shape[1]};
   Tensor *o = nullptr;
   const fg_handle h = c.make(shp, 2, FG_F32, &o);
-  launch_matmul_f32((const float *)at.ptr, (const float *)bt.ptr, (float *)o->ptr, at.shape[0], at.shape[1],
-                    bt.shape[1], c.stream);
+  launch_matmul(c, (const float *)at.ptr, (const float *)bt.ptr, (float *)o->ptr, at.shape[0], at.shape[1],
+                bt.shape[1], false);
   *out = h;
   FG_API_END
 }

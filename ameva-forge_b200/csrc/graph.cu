@@ -484,7 +484,7 @@ fg_handle Exec::exec_node(size_t i, const void *const *inputs, const uint64_t *i
       FG_REQUIRE(w.dtype == FG_F32, FG_ERR_DTYPE, "%s: B must be float32", op.c_str());
       const float *ap = (const float *)c.get(ha).ptr, *wp = (const float *)w.ptr;
       const fg_handle h = new_tensor(n, &o);
-      launch_matmul_f32(ap, wp, (float *)o->ptr, M, K, N, s, /*b_trans=*/true);
+      launch_matmul(c, ap, wp, (float *)o->ptr, M, K, N, /*b_trans=*/true);
       return h;
     }
     Tensor &b = c.get(hb);
@@ -492,7 +492,7 @@ fg_handle Exec::exec_node(size_t i, const void *const *inputs, const uint64_t *i
                op.c_str(), (long long)K, (long long)N);
     const float *ap = (const float *)c.get(ha).ptr, *bq = (const float *)b.ptr;
     const fg_handle h = new_tensor(n, &o);
-    launch_matmul_f32(ap, bq, (float *)o->ptr, M, K, N, s);
+    launch_matmul(c, ap, bq, (float *)o->ptr, M, K, N, false);
     return h;
   }
   if (op == "permute") {  // permute.wgsl.ts; params = dims

@@ -135,6 +135,12 @@ void launch_qmatmul_q4k(const void *w, int64_t N, int64_t K, const float *x, int
 void launch_dequant_q6k(const void *blocks, int64_t n_blocks, float *out, cudaStream_t s);
 void launch_qmatmul_q6k(const void *w, int64_t N, int64_t K, const float *x, int64_t M, float *y, float *scratch,
                         cudaStream_t s);
+// Epilogue pass over k-quant GEMV outputs (q4k.cu): mode 0 = QKV from s0 (q, n0 columns), s1 (k, n1),
+// s2 (v, n1); mode 1 = pair p from (s0[m][p], s1[m][p]) (gate, up); mode 2 = the columns of s0.
+// npairs = output columns / 2.
+struct Epilogue;
+void launch_kq_post(const Epilogue &ep, int M, int64_t npairs, const float *s0, int64_t n0, const float *s1,
+                    int64_t n1, const float *s2, int mode, cudaStream_t s);
 void launch_synth_normal(uint64_t seed, uint64_t offset, int64_t n, float mean, float stdv, int dtype, void *out,
                          cudaStream_t s);
 // Synthetic [N, K] block of a [*, k_full] matrix starting at (row0, col0),
@@ -182,6 +188,14 @@ void launch_qgemm_tc(const QMat &w, const float *x, int M, int64_t ldx, const Ep
 // C[M, N] = A[M, K] B[K, N]; b_trans: B stored as [N, K].
 void launch_matmul_f32(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, cudaStream_t s,
                        bool b_trans = false);
+// matmul_tc.cu: the same product on tcgen05 (tf32 with a three-term split, fp32-level accuracy); `scratch`
+// holds matmul_tc_scratch_bytes(M, K, N).  launch_matmul picks it (or the SIMT kernel for small
+// products) and takes the scratch from the context's pool.
+uint64_t matmul_tc_scratch_bytes(int64_t M, int64_t K, int64_t N);
+void launch_matmul_tc(const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, bool b_trans,
+                      void *scratch, int *err, cudaStream_t s);
+bool matmul_use_tc(int64_t M, int64_t K, int64_t N);
+void launch_matmul(Ctx &c, const float *A, const float *B, float *C, int64_t M, int64_t K, int64_t N, bool b_trans);
 
 // attention.cu
 struct AttnArgs {

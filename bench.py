@@ -344,6 +344,29 @@ def gemm_table(ctx, reps=8, rounds=10):
         for w in ws:
             ctx.dispose(w)
         ctx.synchronize()
+    # fp32 matmul (the reference's matmul / matmul_tiled and fp32 nn.Linear): tcgen05 tf32 with the
+    # three-term split (3 MMA passes); useful flops 2 M N K, event-timed per call incl. the split pass
+    for (M, K, N) in [(2048, 4096, 4096), (512, 4096, 11008)]:
+        a = ctx.synth_normal((M, K), np.float32, seed=5)
+        b = ctx.synth_normal((K, N), np.float32, seed=6)
+        for _ in range(2):
+            ctx.dispose(ctx.matmul(a, b))
+        ctx.synchronize()
+        outs = []
+        with torch.cuda.stream(stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(rounds):
+                outs.append(ctx.matmul(a, b))
+            e1.record()
+        e1.synchronize()
+        us = 1000 * e0.elapsed_time(e1) / rounds
+        fl = 2.0 * M * N * K
+        rows.append({"qtype": "F32", "N": N, "K": K, "batch": M, "kernel": "k_tf32_split + k_matmul_tc (tcgen05 tf32 x3)",
+                     "us": us, "TFLOPs": fl / us / 1e6, "tensor_frac": fl / us / 1e6 / peak_tf})
+        for h in outs + [a, b]:
+            ctx.dispose(h)
+        ctx.synchronize()
     return rows
 
 

@@ -4,6 +4,7 @@ import pytest
 
 import inputs as I
 import oracle as O
+from conftest import max_rel_err
 from forge_b200.errors import AMEVAForgeShapeError, AMEVAForgeValidationError
 
 pytestmark = pytest.mark.gpu
@@ -39,6 +40,27 @@ def test_matmul_golden(ctx, golden, shape):
     A, B = I.matmul(M, K, N)
     out = ctx.read(ctx.matmul(ctx.upload(A), ctx.upload(B)))
     np.testing.assert_allclose(out, golden[f"matmul_{M}x{K}x{N}"], atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("shape", I.MATMUL_SHAPES)
+def test_matmul_golden_tensor_core(ctx, golden, shape, monkeypatch):
+    """The reference's 15 matmul shapes forced onto the tcgen05 tf32 path (three-term split), at the
+    reference suite's tolerance (matmul_tiled.test.ts:146-212: atol 1e-4)."""
+    monkeypatch.setenv("FORGE_B200_MATMUL", "tc")
+    M, K, N = shape
+    A, B = I.matmul(M, K, N)
+    out = ctx.read(ctx.matmul(ctx.upload(A), ctx.upload(B)))
+    np.testing.assert_allclose(out, golden[f"matmul_{M}x{K}x{N}"], atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("M,K,N", [(300, 1000, 257), (1, 4096, 4096), (513, 129, 700), (128, 4096, 384)])
+def test_matmul_tensor_core_vs_oracle(ctx, M, K, N):
+    """Products of at least 2^20 multiply-adds take the tensor-core path by default: ragged tiles in
+    every dimension, K not a multiple of 32, a single row."""
+    A = O.normal(41, 0, M * K).reshape(M, K)
+    B = O.normal(42, 0, K * N).reshape(K, N)
+    out = ctx.read(ctx.matmul(ctx.upload(A), ctx.upload(B)))
+    assert max_rel_err(out, O.matmul(A, B)) <= 1e-5
 
 
 def test_embedding_zero_rows_for_bad_ids(ctx):
