@@ -29,7 +29,8 @@
 // Work per quad is counted in shared-memory instructions: the MMA thread's
 // waits, MMAs and commits queue behind the producers' stores, so both sides
 // work at quad granularity.  When the (weight tile, token tile) grid is
-// smaller than the GPU, K is split over several CTAs (one wave at most): each
+// small against the GPU, K is split over several CTAs (the split count that
+// minimises waves x quads per CTA): each
 // writes its partial tile and the last one of a tile to arrive sums them in
 // split order (deterministic) and runs the epilogue.
 //
@@ -354,8 +355,19 @@ void launch_tc_t(const QMat &w, const float *x, int M, int64_t ldx, const Epilog
   const int nq = (int)w.row_words;  // K split in whole quads, at least 4 per split
   int splits = 1;
   const int tiles = tiles_n * tiles_m;
-  // split K while the CTAs still fit in one wave (a second wave would cost a whole CTA time)
-  if (tiles < num_sms) splits = std::max(1, std::min(num_sms / tiles, nq / 4));
+  // split K to minimise waves x (quads per CTA + a fixed per-CTA cost of about 4 quads: TMEM
+  // allocation, pipeline fill, epilogue, fix-up); e.g. 86 tiles of 32 quads on 148 SMs run 3 splits
+  // in 2 waves (2 x 15) rather than 1 split in 1 wave (36)
+  if (tiles < 2 * num_sms) {
+    int best = (tiles + num_sms - 1) / num_sms * (nq + 4);
+    for (int s = 2; s <= std::min(16, nq / 4); ++s) {
+      const int cost = (tiles * s + num_sms - 1) / num_sms * ((nq + s - 1) / s + 4);
+      if (cost < best) {
+        best = cost;
+        splits = s;
+      }
+    }
+  }
   if (splits > 1) {
     const uint64_t need = (uint64_t)tiles * splits * kTcRows * NT;
     if (need > sc.part_floats || tiles > sc.n_tickets) splits = 1;
