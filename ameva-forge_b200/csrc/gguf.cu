@@ -346,8 +346,10 @@ int fg_gguf_llama_config(const fg_gguf *g, int32_t max_position, int32_t max_bat
   const Tensor *q = g->tensor("blk.0.attn_q.weight");
   FG_REQUIRE(q, FG_ERR_VALIDATION, "GGUF: blk.0.attn_q.weight missing");
   c.qtype = to_fg_type(q->type);
-  FG_REQUIRE(c.qtype == FG_Q4_0 || c.qtype == FG_Q8_0, FG_ERR_DTYPE,
-             "GGUF: the Linear weights must be Q4_0 or Q8_0 (blk.0.attn_q.weight has ggml type %u)", q->type);
+  if (c.qtype == FG_Q6_K) c.qtype = FG_Q4_K;  // a k-quant model: each Linear Q4_K or Q6_K
+  FG_REQUIRE(c.qtype == FG_Q4_0 || c.qtype == FG_Q8_0 || c.qtype == FG_Q4_K, FG_ERR_DTYPE,
+             "GGUF: the Linear weights must be Q4_0, Q8_0 or Q4_K / Q6_K (blk.0.attn_q.weight has ggml type %u)",
+             q->type);
   c.max_position_embeddings =
       max_position > 0 ? max_position : (int32_t)g->num("llama.context_length", 2048, false);
   c.max_batch = max_batch > 0 ? max_batch : 1;
@@ -385,8 +387,10 @@ int fg_llama_load_gguf(fg_llama *m, const fg_gguf *g) {
     if (int st = fg_llama_load(m, as, layer, f.data(), f.size() * 4)) fg::raise(st, "%s", fg::g_last_error.c_str());
   };
   auto load_q = [&](const char *as, int layer, const Tensor &t) {
-    FG_REQUIRE(to_fg_type(t.type) == c.qtype, FG_ERR_DTYPE, "GGUF: %s is ggml type %u, the model's Linears are %s",
-               t.name.c_str(), t.type, c.qtype == FG_Q4_0 ? "Q4_0" : "Q8_0");
+    const int ft = to_fg_type(t.type);
+    const bool ok = c.qtype == FG_Q4_K ? (ft == FG_Q4_K || ft == FG_Q6_K) : ft == c.qtype;
+    FG_REQUIRE(ok, FG_ERR_DTYPE, "GGUF: %s is ggml type %u, the model's Linears are %s", t.name.c_str(), t.type,
+               c.qtype == FG_Q4_0 ? "Q4_0" : c.qtype == FG_Q8_0 ? "Q8_0" : "Q4_K / Q6_K");
     load(as, layer, t);
   };
   {  // the embedding table is kept in fp16

@@ -37,9 +37,18 @@ enum Tid { T_Q = 0, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_ATTN_NORM, T_FFN_NORM
 constexpr int kGlobal = 0xFFFF;
 enum Gid { G_EMBED = 0, G_NORM = 1, G_LM_HEAD = 2 };
 
+// One Linear of a k-quant model (GGUF Q4_K / Q6_K blocks in file order, [N][K]).
+struct KQ {
+  void *p = nullptr;
+  int type = 0;
+  int64_t N = 0, K = 0;
+};
+enum { KQ_Q, KQ_K, KQ_V, KQ_O, KQ_GATE, KQ_UP, KQ_DOWN, KQ_N };
+
 struct LayerW {
   float *attn_norm = nullptr, *ffn_norm = nullptr;
   QMat qkv, o, gateup, down;
+  KQ kq[KQ_N];                        // k-quant models: the Linears as loaded, each of its own type
   __half *k = nullptr, *v = nullptr;  // [max_batch][Hkv_l][cap][d]
 };
 }  // namespace
@@ -71,6 +80,11 @@ struct fg_llama {
   int last_batch = 0;
   std::map<int, cudaGraphExec_t> graphs;
   bool use_step = false;  // batch-1 decode runs the persistent step kernel
+  // k-quant model (created with qtype FG_Q4_K): every Linear is Q4_K or Q6_K as loaded (a llama.cpp
+  // Q4_K_M file mixes both); the layer runs the k-quant GEMVs plus an epilogue pass
+  bool kq = false;
+  KQ lm_kq;
+  float *kq_tmp = nullptr;  // [m_max][max(q + 2 kv, 2 I, H) columns]
   StepArgs step_args{};
   // tensor-parallel exchange region of this rank (cudaMalloc, shared by IPC) and the peers' mappings
   void *xbuf = nullptr;
@@ -154,7 +168,99 @@ AttnArgs attn_args(fg_llama *m, const LayerW &L, int B, int T) {
 // in m->ids ([B][T]); leaves greedy ids of the last position in m->ids[0..B)
 // and advances pos by T.  Everything is enqueued on the context stream (and is
 // graph-capturable when T == 1).
+// y [M][w.N] = x [M][w.K] W^T for a k-quant Linear: the k-quant GEMV for up to 8 rows, else the
+// bit-exact dequantisation into a temporary and the fp32 matmul (tensor cores for large products).
+void kq_linear(fg_llama *m, const KQ &w, const float *x, int M, float *y) {
+  Ctx &c = *m->ctx;
+  FG_REQUIRE(w.p, FG_ERR_VALIDATION, "k-quant model: a Linear of shape [%lld, %lld] was never loaded",
+             (long long)w.N, (long long)w.K);
+  if (M <= 8) {
+    if (w.type == FG_Q4_K)
+      launch_qmatmul_q4k(w.p, w.N, w.K, x, M, y, nullptr, c.stream);
+    else
+      launch_qmatmul_q6k(w.p, w.N, w.K, x, M, y, nullptr, c.stream);
+    return;
+  }
+  const uint64_t bytes = 4ull * (uint64_t)(w.N * w.K);
+  float *w32 = (float *)c.alloc(bytes);
+  try {
+    if (w.type == FG_Q4_K)
+      launch_dequant_q4k(w.p, w.N * w.K / 256, w32, c.stream);
+    else
+      launch_dequant_q6k(w.p, w.N * w.K / 256, w32, c.stream);
+    launch_matmul(c, x, w32, y, M, w.K, w.N, /*b_trans=*/true);
+  } catch (...) {
+    c.free_async(w32, bytes);
+    throw;
+  }
+  c.free_async(w32, bytes);
+}
+
+// forward_tokens of a k-quant model: per Linear the k-quant GEMV (plain output), then the layered
+// path's epilogues as a separate pass (RoPE + fp16 KV append, SwiGLU, residual add).
+void forward_tokens_kq(fg_llama *m, int B, int T, bool log_tokens) {
+  Ctx &c = *m->ctx;
+  const int M = B * T, H = m->H, d = m->d, I = m->I_l;
+  const int64_t nq = (int64_t)m->Hq_l * d, nkv = (int64_t)m->Hkv_l * d;
+  const float eps = m->cfg.rms_norm_eps;
+  launch_embedding(m->embed, 1, m->cfg.vocab_size, H, m->ids, 0, M, m->h, c.stream);
+  Epilogue resid;  // h += W x
+  resid.mode = EPI_PLAIN;
+  resid.y = m->h;
+  resid.resid = m->h;
+  resid.ldy = H;
+  for (size_t l = 0; l < m->layers.size(); ++l) {
+    const LayerW &L = m->layers[l];
+    float *tq = m->kq_tmp, *tk = tq + (int64_t)M * nq, *tv = tk + (int64_t)M * nkv;
+    launch_rmsnorm(m->h, H, L.attn_norm, eps, M, H, m->xn, c.stream);
+    kq_linear(m, L.kq[KQ_Q], m->xn, M, tq);
+    kq_linear(m, L.kq[KQ_K], m->xn, M, tk);
+    kq_linear(m, L.kq[KQ_V], m->xn, M, tv);
+    Epilogue e1;
+    e1.mode = EPI_QKV;
+    e1.q_out = m->q;
+    e1.k_cache = L.k;
+    e1.v_cache = L.v;
+    e1.n_q = (int)nq;
+    e1.n_kv = (int)nkv;
+    e1.head_dim = d;
+    e1.cap = m->cap;
+    e1.tokens_per_seq = T;
+    e1.pos = m->pos;
+    e1.inv_freq = m->inv_freq;
+    launch_kq_post(e1, M, (nq + 2 * nkv) / 2, tq, nq, tk, nkv, tv, 0, c.stream);
+
+    AttnArgs a = attn_args(m, L, B, T);
+    if (T == 1 && attn_decode_supported(a))
+      launch_attention_decode(a, m->decode_splits, m->attn_scratch, c.stream);
+    else
+      launch_attention(a, c.num_sms, c.stream);
+
+    float *to = m->kq_tmp;
+    kq_linear(m, L.kq[KQ_O], m->att, M, to);
+    launch_kq_post(resid, M, H / 2, to, 0, nullptr, 0, nullptr, 2, c.stream);
+
+    launch_rmsnorm(m->h, H, L.ffn_norm, eps, M, H, m->xn, c.stream);
+    float *tg = m->kq_tmp, *tu = tg + (int64_t)M * I;
+    kq_linear(m, L.kq[KQ_GATE], m->xn, M, tg);
+    kq_linear(m, L.kq[KQ_UP], m->xn, M, tu);
+    Epilogue e4;
+    e4.mode = EPI_SWIGLU;
+    e4.y = m->ffn;
+    e4.ldy = I;
+    launch_kq_post(e4, M, I, tg, 0, tu, 0, nullptr, 1, c.stream);
+    kq_linear(m, L.kq[KQ_DOWN], m->ffn, M, to);
+    launch_kq_post(resid, M, H / 2, to, 0, nullptr, 0, nullptr, 2, c.stream);
+  }
+  // lm_head over the last position of every sequence, after the final norm
+  launch_rmsnorm(m->h + (int64_t)(T - 1) * H, (int64_t)T * H, m->norm, eps, B, H, m->xn, c.stream);
+  kq_linear(m, m->lm_kq, m->xn, B, m->logits);
+  launch_argmax(m->logits, B, m->V_l, m->V_l, m->ids, c.stream);
+  launch_advance_pos(m->pos, B, T, log_tokens ? m->token_log : nullptr, m->ids, m->step, m->log_steps, c.stream);
+}
+
 void forward_tokens(fg_llama *m, int B, int T, bool log_tokens) {
+  if (m->kq) return forward_tokens_kq(m, B, T, log_tokens);
   Ctx &c = *m->ctx;
   const int M = B * T;
   const int H = m->H;
@@ -409,7 +515,12 @@ int fg_llama_create(fg_ctx *ctx_h, const fg_llama_config *cfg, fg_llama **out) {
   std::lock_guard<std::recursive_mutex> lk(c.mu);
   FG_CUDA(cudaSetDevice(c.device));
   const fg_llama_config &k = *cfg;
-  FG_REQUIRE(k.qtype == FG_Q4_0 || k.qtype == FG_Q8_0, FG_ERR_DTYPE, "llama: qtype must be Q4_0 or Q8_0");
+  FG_REQUIRE(k.qtype == FG_Q4_0 || k.qtype == FG_Q8_0 || k.qtype == FG_Q4_K, FG_ERR_DTYPE,
+             "llama: qtype must be Q4_0, Q8_0 or Q4_K (a k-quant model whose Linears are Q4_K / Q6_K)");
+  FG_REQUIRE(k.qtype != FG_Q4_K || c.tp_size == 1, FG_ERR_UNSUPPORTED_OP,
+             "llama: k-quant models run on one GPU (no tensor parallelism)");
+  FG_REQUIRE(k.qtype != FG_Q4_K || (k.hidden_size % 256 == 0 && k.intermediate_size % 256 == 0), FG_ERR_SHAPE,
+             "llama: k-quant models need hidden and intermediate sizes that are multiples of 256");
   FG_REQUIRE(k.num_attention_heads > 0 && k.num_key_value_heads > 0 &&
                  k.num_attention_heads % k.num_key_value_heads == 0 && k.hidden_size % k.num_attention_heads == 0,
              FG_ERR_VALIDATION, "num_attention_heads (%d) must be divisible by num_key_value_heads (%d)",
@@ -440,20 +551,23 @@ int fg_llama_create(fg_ctx *ctx_h, const fg_llama_config *cfg, fg_llama **out) {
   m->max_batch = k.max_batch;
   m->m_max = std::max(k.max_batch, 2048);
   const int L = k.num_hidden_layers, H = k.hidden_size, qt = k.qtype;
+  m->kq = qt == FG_Q4_K;
   try {
     m->embed = (__half *)m->dalloc((uint64_t)k.vocab_size * H * 2);
     m->norm = (float *)m->dalloc((uint64_t)H * 4);
-    m->lm_head = make_qmat(m.get(), qt, m->V_l, H);
+    if (!m->kq) m->lm_head = make_qmat(m.get(), qt, m->V_l, H);
     m->layers.resize(L);
     const uint64_t kv_elems = (uint64_t)m->max_batch * m->Hkv_l * m->cap * d;
     for (int l = 0; l < L; ++l) {
       LayerW &w = m->layers[l];
       w.attn_norm = (float *)m->dalloc((uint64_t)H * 4);
       w.ffn_norm = (float *)m->dalloc((uint64_t)H * 4);
-      w.qkv = make_qmat(m.get(), qt, (int64_t)(m->Hq_l + 2 * m->Hkv_l) * d, H);
-      w.o = make_qmat(m.get(), qt, H, (int64_t)m->Hq_l * d);
-      w.gateup = make_qmat(m.get(), qt, 2LL * m->I_l, H);
-      w.down = make_qmat(m.get(), qt, H, m->I_l);
+      if (!m->kq) {
+        w.qkv = make_qmat(m.get(), qt, (int64_t)(m->Hq_l + 2 * m->Hkv_l) * d, H);
+        w.o = make_qmat(m.get(), qt, H, (int64_t)m->Hq_l * d);
+        w.gateup = make_qmat(m.get(), qt, 2LL * m->I_l, H);
+        w.down = make_qmat(m.get(), qt, H, m->I_l);
+      }
       w.k = (__half *)m->dalloc(kv_elems * 2);
       w.v = (__half *)m->dalloc(kv_elems * 2);
       // finite past the live length: the tensor-core attention reads whole 128-key blocks (masked)
@@ -475,6 +589,10 @@ int fg_llama_create(fg_ctx *ctx_h, const fg_llama_config *cfg, fg_llama **out) {
     m->att = (float *)m->dalloc((uint64_t)mm * m->Hq_l * d * 4);
     m->ffn = (float *)m->dalloc((uint64_t)mm * m->I_l * 4);
     m->logits = (float *)m->dalloc((uint64_t)m->max_batch * m->V_l * 4);
+    if (m->kq) {
+      const int64_t cols = std::max<int64_t>(std::max<int64_t>((int64_t)(m->Hq_l + 2 * m->Hkv_l) * d, 2LL * m->I_l), H);
+      m->kq_tmp = (float *)m->dalloc((uint64_t)mm * cols * 4);
+    }
     if (tp > 1) m->logits_all = (float *)m->dalloc((uint64_t)tp * m->max_batch * m->V_l * 4);
     // decode attention scratch, sized for the largest batch and full cache
     const LayerW empty_layer{};
@@ -494,7 +612,7 @@ int fg_llama_create(fg_ctx *ctx_h, const fg_llama_config *cfg, fg_llama **out) {
     // Batch-1 decode runs as one persistent kernel per token where it applies
     // (FORGE_B200_DECODE=layered keeps the per-layer kernels, for comparison).
     const char *mode = std::getenv("FORGE_B200_DECODE");
-    if (!(mode && std::string(mode) == "layered") &&
+    if (!m->kq && !(mode && std::string(mode) == "layered") &&
         decode_step_supported(d, m->Hq_l / m->Hkv_l, qt, H, m->I_l, (int64_t)m->Hq_l * d))
       setup_step(m.get());
   } catch (...) {
@@ -526,6 +644,8 @@ int fg_llama_destroy(fg_llama *m) {
 int fg_llama_synthesize(fg_llama *m, uint64_t seed, float stdv) {
   FG_LAPI_BEGIN
   LGuard g(m);
+  FG_REQUIRE(!m->kq, FG_ERR_UNSUPPORTED_OP,
+             "llama: a k-quant model loads its Linears (fg_llama_load / fg_llama_load_gguf); no synthetic recipe");
   Ctx &c = *m->ctx;
   const auto &k = m->cfg;
   const int H = k.hidden_size, d = m->d, qt = k.qtype, r = m->rank;
@@ -587,6 +707,39 @@ int fg_llama_load(fg_llama *m, const char *name, int32_t layer, const void *host
   };
   const int nq = m->Hq_l * d, nkv = m->Hkv_l * d;
   const int Hq = k.num_attention_heads, Hkv = k.num_key_value_heads;
+  if (m->kq && n != "embed" && n != "norm" && n != "attn_norm" && n != "ffn_norm") {
+    // a k-quant Linear, as GGUF Q4_K or Q6_K blocks: the type follows from the byte count
+    KQ *w = nullptr;
+    int64_t N = 0, K = H;
+    if (n == "lm_head") {
+      w = &m->lm_kq, N = k.vocab_size;
+    } else {
+      FG_REQUIRE(layer >= 0 && layer < k.num_hidden_layers, FG_ERR_VALIDATION, "%s: layer %d out of range",
+                 n.c_str(), layer);
+      LayerW &L = m->layers[layer];
+      if (n == "q") w = &L.kq[KQ_Q], N = nq;
+      else if (n == "k") w = &L.kq[KQ_K], N = nkv;
+      else if (n == "v") w = &L.kq[KQ_V], N = nkv;
+      else if (n == "o") w = &L.kq[KQ_O], N = H, K = nq;
+      else if (n == "gate") w = &L.kq[KQ_GATE], N = m->I_l;
+      else if (n == "up") w = &L.kq[KQ_UP], N = m->I_l;
+      else if (n == "down") w = &L.kq[KQ_DOWN], N = H, K = m->I_l;
+      else raise(FG_ERR_VALIDATION, "unknown weight name '%s'", n.c_str());
+    }
+    const uint64_t sb = (uint64_t)N * (K / 256);
+    const int type = bytes == sb * 144 ? FG_Q4_K : bytes == sb * 210 ? FG_Q6_K : -1;
+    FG_REQUIRE(type >= 0 && K % 256 == 0, FG_ERR_SHAPE,
+               "%s: a k-quant model takes Q4_K (%llu bytes) or Q6_K (%llu bytes) blocks of [%lld, %lld], got %llu",
+               n.c_str(), (unsigned long long)(sb * 144), (unsigned long long)(sb * 210), (long long)N, (long long)K,
+               (unsigned long long)bytes);
+    if (!w->p || w->type != type) w->p = m->dalloc(bytes);
+    w->type = type;
+    w->N = N;
+    w->K = K;
+    c.h2d(w->p, host, bytes);
+    c.sync();
+    return FG_OK;
+  }
   if (n == "embed") {
     FG_REQUIRE(bytes == (uint64_t)k.vocab_size * H * 2, FG_ERR_SHAPE, "embed: expected float16 [%d, %d]", k.vocab_size, H);
     c.h2d(m->embed, host, bytes);
@@ -757,9 +910,13 @@ int fg_llama_decode(fg_llama *m, const int32_t *ids, int32_t batch, int32_t *nex
   Ctx &c = *m->ctx;
   FG_REQUIRE(batch >= 1 && batch <= m->max_batch, FG_ERR_SHAPE, "batch %d outside [1, %d]", batch, m->max_batch);
   FG_REQUIRE(m->host_pos + 1 <= m->cap, FG_ERR_SHAPE, "KV cache capacity %d exceeded", m->cap);
-  cudaGraphExec_t exec = decode_graph(m, batch);
   if (ids) c.h2d(m->ids, ids, (uint64_t)batch * 4);
-  FG_CUDA(cudaGraphLaunch(exec, c.stream));
+  if (m->kq) {  // launched directly: the k-quant path may take pool scratch, which a captured graph cannot
+    forward_tokens(m, batch, 1, true);
+  } else {
+    cudaGraphExec_t exec = decode_graph(m, batch);
+    FG_CUDA(cudaGraphLaunch(exec, c.stream));
+  }
   m->host_pos += 1;
   m->last_batch = batch;
   if (logits) read_logits(m, batch, logits);
@@ -775,9 +932,13 @@ int fg_llama_generate_device(fg_llama *m, int32_t batch, int32_t steps) {
   FG_REQUIRE(batch >= 1 && batch <= m->max_batch, FG_ERR_SHAPE, "batch %d outside [1, %d]", batch, m->max_batch);
   FG_REQUIRE(steps >= 0 && steps <= m->log_steps, FG_ERR_SHAPE, "steps %d outside [0, %d]", steps, m->log_steps);
   FG_REQUIRE(m->host_pos + steps <= m->cap, FG_ERR_SHAPE, "KV cache capacity %d exceeded", m->cap);
-  cudaGraphExec_t exec = decode_graph(m, batch);
   FG_CUDA(cudaMemsetAsync(m->step, 0, 4, c.stream));
-  for (int s = 0; s < steps; ++s) FG_CUDA(cudaGraphLaunch(exec, c.stream));
+  if (m->kq) {
+    for (int s = 0; s < steps; ++s) forward_tokens(m, batch, 1, true);
+  } else {
+    cudaGraphExec_t exec = decode_graph(m, batch);
+    for (int s = 0; s < steps; ++s) FG_CUDA(cudaGraphLaunch(exec, c.stream));
+  }
   m->host_pos += steps;
   m->last_batch = batch;
   FG_LAPI_END

@@ -21,6 +21,7 @@
 // super-blocks per stage (16-byte cp.async copies), so ~3.4 KB per warp are
 // in flight without holding registers.  HBM-bound: 144 bytes per 256 weights.  Larger M dequantises the
 // matrix once and runs the fp32 GEMM.
+#include "epilogue.cuh"
 #include "runtime.cuh"
 #include "tma.cuh"
 
@@ -343,6 +344,54 @@ void launch_qmatmul_q4k(const void *w, int64_t N, int64_t K, const float *x, int
       launch_dequant_q4k(w, N * K / 256, scratch, s);
       launch_matmul_f32(x, scratch, y, M, K, N, s, /*b_trans=*/true);
   }
+}
+
+// ---------------------------------------------------------------------------
+// Epilogue pass of a k-quant model layer.  The k-quant GEMVs write plain
+// [M][N] outputs, so RoPE + fp16 KV append, SwiGLU and the residual add run
+// as a second pass through the same epi_store_pair the fused Q4_0 kernels
+// call, on the pair (v0, v1) of output columns (n, n + 1):
+//  * QKV: columns [0, n0) of s0 (q), [n0, n0 + n1) of s1 (k), then s2 (v);
+//  * interleave: pair p is (s0[m][p], s1[m][p]) at column 2p (gate, up);
+//  * plain: columns of s0.
+// ---------------------------------------------------------------------------
+__global__ void k_kq_post(Epilogue ep, int M, int64_t npairs, const float *s0, int64_t n0, const float *s1,
+                          int64_t n1, const float *s2, int mode) {
+  const int64_t total = (int64_t)M * npairs;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / npairs);
+    const int64_t p = i % npairs;
+    float v0, v1;
+    int64_t n;
+    if (mode == 1) {  // interleave
+      v0 = s0[(int64_t)m * npairs + p];
+      v1 = s1[(int64_t)m * npairs + p];
+      n = 2 * p;
+    } else {
+      n = 2 * p;
+      const float *src;
+      int64_t col, ld;
+      if (mode == 0 && n >= n0 + n1) {
+        src = s2, col = n - n0 - n1, ld = n1;
+      } else if (mode == 0 && n >= n0) {
+        src = s1, col = n - n0, ld = n1;
+      } else {
+        src = s0, col = n, ld = mode == 0 ? n0 : 2 * npairs;
+      }
+      v0 = src[(int64_t)m * ld + col];
+      v1 = src[(int64_t)m * ld + col + 1];
+    }
+    epi_store_pair(ep, n, m, v0, v1);
+  }
+}
+
+void launch_kq_post(const Epilogue &ep, int M, int64_t npairs, const float *s0, int64_t n0, const float *s1,
+                    int64_t n1, const float *s2, int mode, cudaStream_t s) {
+  const int64_t total = (int64_t)M * npairs;
+  if (total == 0) return;
+  const int grid = (int)std::min<int64_t>(ceil_div(total, 256), 148 * 16);
+  k_kq_post<<<grid, 256, 0, s>>>(ep, M, npairs, s0, n0, s1, n1, s2, mode);
+  FG_LAUNCH_CHECK();
 }
 
 }  // namespace fg

@@ -77,4 +77,4 @@ class GGUFFile:
                            num_key_value_heads=c.num_key_value_heads,
                            max_position_embeddings=c.max_position_embeddings, rms_norm_eps=c.rms_norm_eps,
                            rope_theta=c.rope_theta, max_batch=c.max_batch,
-                           qtype={16: "Q4_0", 17: "Q8_0"}[c.qtype])
+                           qtype={16: "Q4_0", 17: "Q8_0", 18: "Q4_K"}[c.qtype])

@@ -432,6 +432,32 @@ def synth_llama(shape: LlamaShape, seed: int, qtype: int = Q4_0, std: float = 0.
     return w
 
 
+# A k-quant model in the type mix of a llama.cpp Q4_K_M file: Q6_K for attn_v, ffn_down and the output
+# matrix, Q4_K for the other Linears.  Each Linear is (type name, GGUF blocks); embedding and norms follow
+# synth_llama's recipe.
+KQ_MIX = {"q": "Q4_K", "k": "Q4_K", "v": "Q6_K", "o": "Q4_K", "gate": "Q4_K", "up": "Q4_K", "down": "Q6_K"}
+
+
+def kquant_llama(shape: LlamaShape, seed: int, d_scale: float = 1e-4) -> LlamaWeights:
+    H, I, V = shape.hidden_size, shape.intermediate_size, shape.vocab_size
+    kvd = shape.num_key_value_heads * shape.head_dim
+    emb = f32_to_f16(synth_matrix(seed, GLOBAL_LAYER, GID["embed"], V, H, 0.02))
+    norm = normal(tensor_seed(seed, GLOBAL_LAYER, GID["norm"]), 0, H, 1.0, 0.1)
+    rnd = {"Q4_K": random_q4k, "Q6_K": random_q6k}
+    lm = ("Q6_K", random_q6k(V, H, tensor_seed(seed, GLOBAL_LAYER, GID["lm_head"]) & 0xFFFFFFFF, d_scale))
+    w = LlamaWeights(shape, -1, emb, norm, lm)
+    dims = {"q": (H, H), "k": (kvd, H), "v": (kvd, H), "o": (H, H), "gate": (I, H), "up": (I, H), "down": (H, I)}
+    for l in range(shape.num_hidden_layers):
+        L = {}
+        for name, (r, c) in dims.items():
+            t = KQ_MIX[name]
+            L[name] = (t, rnd[t](r, c, tensor_seed(seed, l, TID[name]) & 0xFFFFFFFF, d_scale))
+        L["attn_norm"] = normal(tensor_seed(seed, l, TID["attn_norm"]), 0, H, 1.0, 0.1)
+        L["ffn_norm"] = normal(tensor_seed(seed, l, TID["ffn_norm"]), 0, H, 1.0, 0.1)
+        w.layers.append(L)
+    return w
+
+
 class LlamaRef:
     """numpy restatement of LlamaForCausalLM (packages/forge-py/src/forge/
     models/llama.py:69-248) over quantized weights: pre-norm decoder, KV
@@ -464,6 +490,9 @@ class LlamaRef:
         self.pos = length
 
     def _lin(self, blocks, N, K, x):
+        if isinstance(blocks, tuple):  # a k-quant Linear: (type name, GGUF blocks)
+            t, b = blocks
+            return qmatmul_q4k(b, N, K, x) if t == "Q4_K" else qmatmul_q6k(b, N, K, x)
         return qmatmul(self.w.qtype, blocks, N, K, x)
 
     def forward(self, ids: np.ndarray) -> np.ndarray:

@@ -5,7 +5,8 @@ import struct
 
 import numpy as np
 
-GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0 = 0, 1, 2, 8
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q4_K, GGML_Q6_K = 0, 1, 2, 8, 12, 14
+KQ_GGML = {"Q4_K": GGML_Q4_K, "Q6_K": GGML_Q6_K}
 V_U32, V_F32, V_STR, V_ARR = 4, 6, 8, 9
 
 
@@ -48,7 +49,8 @@ def write(path, meta, tensors, alignment=32, version=3):
 
 
 def write_llama(path, w, context_length=256):
-    """The oracle's LlamaWeights (GGUF Q4_0/Q8_0 blocks, fp16 embedding, fp32 gains)."""
+    """The oracle's LlamaWeights (GGUF Q4_0/Q8_0 blocks, or per-Linear (k-quant type, blocks) pairs of
+    oracle.kquant_llama; fp16 embedding, fp32 gains)."""
     s = w.shape
     H, I, V, d = s.hidden_size, s.intermediate_size, s.vocab_size, s.head_dim
     qt = GGML_Q4_0 if w.qtype == 4 else GGML_Q8_0
@@ -63,7 +65,7 @@ def write_llama(path, w, context_length=256):
     kvd = s.num_key_value_heads * d
     t = [("token_embd.weight", GGML_F16, (H, V), w.embed_f16),
          ("output_norm.weight", GGML_F32, (H,), w.norm.astype(np.float32)),
-         ("output.weight", qt, (H, V), w.lm_head)]
+         ("output.weight", *_lin(qt, (H, V), w.lm_head))]
     names = {"q": ("attn_q", (H, H)), "k": ("attn_k", (H, kvd)), "v": ("attn_v", (H, kvd)),
              "o": ("attn_output", (H, H)), "gate": ("ffn_gate", (H, I)), "up": ("ffn_up", (H, I)),
              "down": ("ffn_down", (I, H))}
@@ -71,5 +73,13 @@ def write_llama(path, w, context_length=256):
         t.append((f"blk.{l}.attn_norm.weight", GGML_F32, (H,), L["attn_norm"].astype(np.float32)))
         t.append((f"blk.{l}.ffn_norm.weight", GGML_F32, (H,), L["ffn_norm"].astype(np.float32)))
         for k, (gname, dims) in names.items():
-            t.append((f"blk.{l}.{gname}.weight", qt, dims, L[k]))
+            t.append((f"blk.{l}.{gname}.weight", *_lin(qt, dims, L[k])))
     write(path, meta, t)
+
+
+def _lin(qt, dims, blocks):
+    """(ggml type, dims, raw bytes) of a Linear: a k-quant (type name, blocks) pair, or blocks of the
+    model's Q4_0 / Q8_0 type."""
+    if isinstance(blocks, tuple):
+        return KQ_GGML[blocks[0]], dims, blocks[1]
+    return qt, dims, blocks

@@ -63,7 +63,8 @@ def test_q4k_upload_roundtrip_and_exact_dequant(ctx):
 @pytest.mark.parametrize("M,N,K", [(1, 200, 2048), (3, 200, 2048), (8, 200, 2048), (12, 200, 2048),
                                    # 43 super-blocks per row: the cp.async ring wraps five times and its last
                                    # stage is partial (43 = 5 x 8 + 3)
-                                   (1, 136, 11008), (4, 136, 11008), (1, 72, 8448)])
+                                   (1, 136, 11008), (4, 136, 11008), (1, 72, 8448),
+                                   (64, 512, 4096)])  # dequant + the tensor-core matmul (transposed B)
 def test_q4k_qmatmul(ctx, M, N, K):
     blocks = O.random_q4k(N, K, 7 + M)
     x = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
@@ -135,7 +136,8 @@ def test_q6k_upload_roundtrip_and_exact_dequant(ctx):
 @pytest.mark.parametrize("M,N,K", [(1, 200, 2048), (3, 200, 2048), (8, 200, 2048), (12, 200, 2048),
                                    # >= 32 super-blocks per row take the 8-in-flight loop; 43 and 33 leave
                                    # tails of 3 and 1 super-blocks
-                                   (1, 136, 11008), (4, 136, 11008), (1, 72, 8448)])
+                                   (1, 136, 11008), (4, 136, 11008), (1, 72, 8448),
+                                   (64, 512, 4096)])
 def test_q6k_qmatmul(ctx, M, N, K):
     blocks = O.random_q6k(N, K, 17 + M)
     x = np.random.default_rng(M).standard_normal((M, K)).astype(np.float32)
