@@ -80,9 +80,9 @@ __device__ __forceinline__ void produce(const CUtensorMap *tq, const CUtensorMap
 // ---------------------------------------------------------------------------
 // Q4_0 tensor-core GEMV (q4_gemv.cuh): a CTA owns consecutive 16-row strips.
 // ---------------------------------------------------------------------------
-constexpr int kQ4Stages = 4;
-
-template <int MV>
+// Ring depth: 4 stages, or 3 where 4 would keep the x staging of a long K from fitting two CTAs per
+// SM (108 KB in flight per SM still streams at full HBM speed).
+template <int MV, int kQ4Stages>
 __global__ void __launch_bounds__(kThreads, 2)
     k_qgemv_q4(QMat w, const float *__restrict__ x, int64_t ldx, const float *__restrict__ gamma, float eps, int do_norm,
                Epilogue ep, GemvScratch scr) {
@@ -321,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-size_t q4_smem(int64_t K, int MV) {
+size_t q4_smem(int64_t K, int MV, int stages = 4) {
   const int nbx = (int)q4_quads(K) * 4;
   size_t xbytes = 0;
   switch (MV) {
@@ -330,7 +330,7 @@ size_t q4_smem(int64_t K, int MV) {
     case 3: xbytes = Q4X<3>::bytes(nbx); break;
     default: xbytes = Q4X<4>::bytes(nbx); break;
   }
-  return 128 + (size_t)kQ4Stages * kQ4TileBytes + xbytes + (size_t)kGroupWarps * kQ4StripRows * MV * 4;
+  return 128 + (size_t)stages * kQ4TileBytes + xbytes + (size_t)kGroupWarps * kQ4StripRows * MV * 4;
 }
 size_t q8_smem(int64_t K, int MV) {
   return 128 + (size_t)kStages * Geo<kRows, kTileBytes, 16>::SB + (size_t)MV * K * 4 + (size_t)kRows * MV * 4;
@@ -349,7 +349,9 @@ void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, f
   const int64_t nb = w.K / 32, nc = q4 ? 1 : ceil_div(nb, CB), G = q4 ? q4_strips(w.N) : ceil_div(w.N, ROWS);
   const int64_t U = G * nc;
   FG_REQUIRE(U < (1ll << 31), FG_ERR_SHAPE, "gemv: matrix too large");
-  const size_t smem = q4 ? q4_smem(w.K, MV) : q8_smem(w.K, MV);
+  // Q4_0: a 3-stage ring where only that keeps two CTAs per SM
+  const int stages = q4 && q4_smem(w.K, MV, 4) > kSmemTwo && q4_smem(w.K, MV, 3) <= kSmemTwo ? 3 : 4;
+  const size_t smem = q4 ? q4_smem(w.K, MV, stages) : q8_smem(w.K, MV);
   const int P = (int)std::min<int64_t>((smem <= kSmemTwo ? 2LL : 1LL) * num_sms, U);
   GemvScratch scx = sc;
   if (!q4) {  // stream-K fix-up slots of the Q8_0 kernel
@@ -360,15 +362,18 @@ void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, f
                "gemv: workspace too small for N=%lld K=%lld", (long long)w.N, (long long)w.K);
     scx.maxc = maxc;
   }
-  static unsigned long long attr_set[2] = {0, 0};  // per instantiation, one bit per device
+  static unsigned long long attr_set[3] = {0, 0, 0};  // per instantiation, one bit per device
+  const int inst = q4 ? (stages == 3 ? 2 : 1) : 0;
   int dev = 0;
   FG_CUDA(cudaGetDevice(&dev));
-  if (!(attr_set[q4] & (1ull << dev))) {
-    if (q4)
-      FG_CUDA(cudaFuncSetAttribute(k_qgemv_q4<MV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOne));
+  if (!(attr_set[inst] & (1ull << dev))) {
+    if (inst == 1)
+      FG_CUDA(cudaFuncSetAttribute(k_qgemv_q4<MV, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOne));
+    else if (inst == 2)
+      FG_CUDA(cudaFuncSetAttribute(k_qgemv_q4<MV, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOne));
     else
       FG_CUDA(cudaFuncSetAttribute(k_qgemv_q8<MV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOne));
-    attr_set[q4] |= 1ull << dev;
+    attr_set[inst] |= 1ull << dev;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)P);
@@ -382,7 +387,10 @@ void launch_mv(const QMat &w, const float *x, int64_t ldx, const float *gamma, f
   cfg.numAttrs = 1;
   if (q4) {
     FG_REQUIRE(((uintptr_t)w.qs & 15) == 0, FG_ERR_VALIDATION, "gemv: Q4_0 tiles must be 16-byte aligned");
-    FG_CUDA(cudaLaunchKernelEx(&cfg, k_qgemv_q4<MV>, w, x, ldx, gamma, eps, do_norm ? 1 : 0, ep, scx));
+    if (stages == 3)
+      FG_CUDA(cudaLaunchKernelEx(&cfg, k_qgemv_q4<MV, 3>, w, x, ldx, gamma, eps, do_norm ? 1 : 0, ep, scx));
+    else
+      FG_CUDA(cudaLaunchKernelEx(&cfg, k_qgemv_q4<MV, 4>, w, x, ldx, gamma, eps, do_norm ? 1 : 0, ep, scx));
   } else {
     const CUtensorMap tq = make_tmap_2d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, w.N, w.row_words, w.row_words * 4,
                                         ROWS, TB / 4);
