@@ -9,7 +9,8 @@
 //                  shared memory, 4 threads per query row.
 // k_attn_decode -- split-KV decode (N_q = 1) over the fp16 KV cache: each
 //                  CTA streams one slice of one KV head for all of its G query
-//                  heads with double-buffered cp.async tiles; the last CTA of a
+//                  heads with a three-stage ring of cp.async tiles per warp
+//                  (two 32-key tiles in flight while one is computed); the last CTA of a
 //                  head (atomic ticket) merges the slices, so no second launch.
 #include "runtime.cuh"
 
@@ -153,16 +154,18 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+constexpr int kDecodeStages = 3;  // cp.async ring depth per warp of k_attn_decode
+
 template <int D, int G>
 __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a, int splits, float *__restrict__ part,
                                                      int *__restrict__ counters) {
-  constexpr int W = 4, T = 32;
+  constexpr int W = 4, T = 32, NS = kDecodeStages;
   constexpr int CH = D / 8;            // 16-byte chunks per row
   constexpr int RPI = 32 / CH;         // rows per warp-instruction in the tile copy
   constexpr int CPL = D / 32;          // output columns per lane
   extern __shared__ __align__(16) unsigned char smraw[];
-  __half *kv = reinterpret_cast<__half *>(smraw);           // [W][2][2][T][D]
-  float *qs = reinterpret_cast<float *>(kv + W * 2 * 2 * T * D);  // [G][D]
+  __half *kv = reinterpret_cast<__half *>(smraw);           // [W][NS][2][T][D]
+  float *qs = reinterpret_cast<float *>(kv + W * NS * 2 * T * D);  // [G][D]
   float *ps = qs + G * D;                                   // [W][G][T]
   __shared__ int s_last;
 
@@ -186,7 +189,7 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a, int splits, flo
 
   const __half *kbase = reinterpret_cast<const __half *>(a.k) + (int64_t)b * a.kv_sb + (int64_t)hk * a.kv_sh;
   const __half *vbase = reinterpret_cast<const __half *>(a.v) + (int64_t)b * a.kv_sb + (int64_t)hk * a.kv_sh;
-  __half *wk = kv + warp * 2 * 2 * T * D;  // this warp's stages
+  __half *wk = kv + warp * NS * 2 * T * D;  // this warp's stages
 
   auto issue = [&](int t, int stage) {
     const int key0 = s0 + t * T;
@@ -213,11 +216,15 @@ __global__ void __launch_bounds__(128) k_attn_decode(AttnArgs a, int splits, flo
     for (int c = 0; c < CPL; ++c) o[g][c] = 0.0f;
   }
 
+  static_assert(NS == 3, "the waits below assume three stages");
   if (t0 < t1) issue(t0, 0);
+  if (t0 + 1 < t1) issue(t0 + 1, 1);
   for (int t = t0; t < t1; ++t) {
-    const int stage = (t - t0) & 1;
-    if (t + 1 < t1) {
-      issue(t + 1, stage ^ 1);
+    const int stage = (t - t0) % NS;
+    if (t + 2 < t1) {  // the stage of tile t + 2 held tile t - 1, finished before the last __syncwarp
+      issue(t + 2, (t - t0 + 2) % NS);
+      cp_async_wait<2>();
+    } else if (t + 1 < t1) {
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
@@ -391,7 +398,8 @@ void launch_simt_t(const AttnArgs &a, cudaStream_t s) {
 
 template <int D, int G>
 void launch_decode_t(const AttnArgs &a, int splits, void *scratch, cudaStream_t s) {
-  const size_t smem = (size_t)4 * 2 * 2 * 32 * D * sizeof(__half) + (size_t)(G * D + 4 * G * 32) * sizeof(float);
+  const size_t smem =
+      (size_t)4 * kDecodeStages * 2 * 32 * D * sizeof(__half) + (size_t)(G * D + 4 * G * 32) * sizeof(float);
   static unsigned long long attr_set = 0;
   int dev = 0;
   FG_CUDA(cudaGetDevice(&dev));
@@ -456,11 +464,26 @@ bool attn_decode_supported(const AttnArgs &a) {
   return a.Nq == 1 && a.kv_f16 && !a.q_f16 && (a.d == 64 || a.d == 128) && (g == 1 || g == 2 || g == 4 || g == 8);
 }
 
-int attn_decode_splits(const AttnArgs &a, int max_kv, int num_sms) {
+int attn_decode_splits(const AttnArgs &a, int max_kv, int num_sms, uint64_t max_scratch) {
   const int64_t heads = (int64_t)a.B * a.Hkv;
-  int splits = (int)std::max<int64_t>(1, ceil_div(2LL * num_sms, heads));
-  splits = (int)std::min<int64_t>(splits, std::max<int64_t>(1, ceil_div(max_kv, 128)));
-  return splits;
+  const int G = a.H / a.Hkv;
+  // resident CTAs per SM from k_attn_decode's shared memory (+ 1 KB the runtime reserves per CTA)
+  const int64_t smem = (int64_t)4 * kDecodeStages * 2 * 32 * a.d * 2 + (int64_t)(G * a.d + 4 * G * 32) * 4 + 1024;
+  const int64_t slots = (int64_t)std::max(1, num_sms) * std::max<int64_t>(1, std::min<int64_t>(16, 233472 / smem));
+  // cost of s splits: waves of equal CTAs x (keys per split + ~64 keys of per-CTA latency); at least 128
+  // keys per split
+  const int cap = (int)std::max<int64_t>(1, ceil_div(max_kv, 128));
+  int best = 1;
+  double best_cost = 0.0;
+  for (int sp = 1; sp <= cap; ++sp) {
+    if (sp > 1 && attn_decode_scratch_bytes(a, sp) > max_scratch) break;
+    const double cost = (double)ceil_div(heads * sp, slots) * (double)(ceil_div(max_kv, sp) + 64);
+    if (sp == 1 || cost < best_cost) {
+      best = sp;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 uint64_t attn_decode_scratch_bytes(const AttnArgs &a, int splits) {

@@ -116,7 +116,7 @@ extern "C" int fg_attention_decode_static(const float *q, const void *k_cache, c
     FG_CUDA(cudaGetDevice(&dev));
     int num_sms = 0;
     void *scratch = scratch_address(dev, &num_sms);
-    const int splits = attn_decode_splits(a, n_kv, num_sms);
+    const int splits = attn_decode_splits(a, n_kv, num_sms, kStaticScratchBytes);
     const uint64_t need = attn_decode_scratch_bytes(a, splits);
     FG_REQUIRE(need <= kStaticScratchBytes, FG_ERR_VALIDATION,
                "attention_decode_static: batch %d x kv_heads %d x %d splits needs %llu bytes of scratch; the static "

@@ -227,7 +227,9 @@ bool attn_decode_supported(const AttnArgs &a);
 // area of attn_decode_scratch_bytes() bytes: per-head arrival counters first
 // (sized for scratch_batch, zero on entry and left zero on exit), then the
 // per-split partial results.
-int attn_decode_splits(const AttnArgs &a, int max_kv, int num_sms);
+// Split count for k_attn_decode: the fewest waves of resident CTAs, weighed
+// against per-CTA latency, within `max_scratch` bytes of scratch.
+int attn_decode_splits(const AttnArgs &a, int max_kv, int num_sms, uint64_t max_scratch = ~0ull);
 uint64_t attn_decode_scratch_bytes(const AttnArgs &a, int splits);
 void launch_attention_decode(const AttnArgs &a, int splits, void *scratch, cudaStream_t s);
 
