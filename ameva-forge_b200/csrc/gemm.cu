@@ -151,7 +151,7 @@ __global__ void __launch_bounds__(256) k_matmul_f32(const float *__restrict__ A,
 void launch_qgemm(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, const GemvScratch &sc,
                   int num_sms, cudaStream_t s) {
   if (M == 0 || w.N == 0) return;
-  // Q4_0 runs on the tensor cores; FORGE_B200_GEMM=simt keeps the CUDA-core kernel (for comparison)
+  // Q4_0 and Q8_0 run on the tensor cores; FORGE_B200_GEMM=simt keeps the CUDA-core kernel (for comparison)
   static const bool force_simt = [] {
     const char *e = std::getenv("FORGE_B200_GEMM");
     return e && std::string(e) == "simt";

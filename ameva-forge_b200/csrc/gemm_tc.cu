@@ -61,17 +61,24 @@ constexpr int kTcMaxRing = 16;
 //  * B: the quad's two 64-column chunks of X, [2][NT][64] fp16 swizzled (one 3-D box);
 //  * A: the quad's dequantised weights, [2][128][64] fp16 swizzled (producer warps);
 //  * raw: the quad of the tile's 8 strips (9 KB, one 3-D box).
-template <int NT>
+//  Q8_0 (QT = FG_Q8_0, NT <= 128): the raw quad is the tile's 128 rows x 128 int8 codes (16 KB, one
+//  2-D box) and their 8-scale groups (2 KB, one 2-D box of the scales of two quads).
+constexpr int kTcQ8CodeBytes = kTcRows * 128, kTcQ8RawBytes = kTcQ8CodeBytes + kTcRows * 16;
+
+template <int NT, int QT = FG_Q4_0>
 struct TcGeo {
+  static constexpr bool Q8 = QT == FG_Q8_0;
+  static constexpr int RawBytes = Q8 ? kTcQ8RawBytes : kTcRawBytes;
   static constexpr int BQuad = 2 * NT * kTcK * 2;  // B bytes per quad
   static constexpr int RB = NT <= 16 ? 16 : NT <= 32 ? 8 : NT <= 64 ? 5 : NT <= 128 ? 3 : 2;
-  static constexpr int SA = NT <= 128 ? 3 : 2;
-  static constexpr int RAW = NT <= 32 ? 6 : NT <= 64 ? 4 : 3;
+  static constexpr int SA = Q8 ? (NT >= 64 ? 2 : 3) : NT <= 128 ? 3 : 2;
+  static constexpr int RAW = Q8 ? 3 : NT <= 32 ? 6 : NT <= 64 ? 4 : 3;
   static constexpr int TmemCols = NT < 32 ? 32 : NT;  // allocation: a power of two >= 32
   static constexpr size_t AOff = (size_t)RB * BQuad;
   static constexpr size_t RawOff = AOff + (size_t)SA * kTcAQuad;
   // + 1 KB for the 1024-byte alignment of the swizzled tiles
-  static constexpr size_t Smem = 1024 + RawOff + (size_t)RAW * kTcRawBytes;
+  static constexpr size_t Smem = 1024 + RawOff + (size_t)RAW * RawBytes;
+  static_assert(!Q8 || NT <= 128, "Q8_0 token tiles up to 128");
   static_assert(RB <= kTcMaxRing && SA <= kTcMaxRing && RAW <= kTcMaxRing && Smem + 1024 <= 232448,
                 "shared memory per CTA");
   static_assert(RawOff >= (size_t)NT * kTcRows * 4, "the epilogue tile reuses the B and A rings");
@@ -119,11 +126,27 @@ __global__ void k_x_to_f16(const float *__restrict__ x, int64_t ldx, int M, int6
   }
 }
 
-template <int NT>
+// Q8_0: eight int8 codes -> four fp16 pairs q * d: 0x6400 | (code ^ 0x80) is 1024 + q + 128 exactly,
+// one exact subtraction leaves q, one multiply by d rounds once.
+__device__ __forceinline__ uint4 dq8(uint2 c, __half2 d2) {
+  const uint32_t u0 = c.x ^ 0x80808080u, u1 = c.y ^ 0x80808080u;
+  const uint32_t h[4] = {__byte_perm(u0, 0x64646464u, 0x4140), __byte_perm(u0, 0x64646464u, 0x4342),
+                         __byte_perm(u1, 0x64646464u, 0x4140), __byte_perm(u1, 0x64646464u, 0x4342)};
+  const __half2 off = __float2half2_rn(1152.0f);
+  uint32_t r[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 t = __hmul2(__hsub2(*reinterpret_cast<const __half2 *>(&h[i]), off), d2);
+    r[i] = *reinterpret_cast<const uint32_t *>(&t);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+template <int NT, int QT>
 __global__ void __launch_bounds__(kTcThreads, 1)
-    k_qgemm_tc(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw, QMat w, int M,
-               Epilogue ep, GemvScratch scr, int splits) {
-  using Geo = TcGeo<NT>;
+    k_qgemm_tc(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+               const __grid_constant__ CUtensorMap tms, QMat w, int M, Epilogue ep, GemvScratch scr, int splits) {
+  using Geo = TcGeo<NT, QT>;
   extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
   unsigned char *sm = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
   constexpr int RB = Geo::RB, SA = Geo::SA, R = Geo::RAW;
@@ -135,7 +158,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int tile_n = blockIdx.x, tile_m = blockIdx.y, split = blockIdx.z;
-  const int nq = (int)w.row_words;
+  const int nq = Geo::Q8 ? (int)((w.K + 127) / 128) : (int)w.row_words;
   // this split's quads (128-wide K chunks, zero-padded at the end of a row)
   const int q0 = (int)((int64_t)split * nq / splits), q1 = (int)((int64_t)(split + 1) * nq / splits);
   const int nquads = q1 - q0;
@@ -167,7 +190,40 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   bool ok = true;
-  if (warp < kTcProducerWarps) {
+  if (Geo::Q8 && warp < kTcProducerWarps) {
+    // ================= Q8_0 producers: warp w dequantises rows 16w .. 16w+15 =================
+    // lane -> (row parity rp, 16-byte output chunk c = 8 codes): 16 lanes read one row's 128 code
+    // bytes and write its two swizzled 128-byte rows; a quad's scale sits at 4 (quad & 1) + c / 4
+    const int rp = lane >> 4, c = lane & 15;
+    for (int qi = 0; qi < nquads; ++qi) {
+      const int rs = qi % R, as = qi % SA, sq = 4 * ((q0 + qi) & 1) + (c >> 2);
+      ok = ok && mbar_wait(&rfull[rs], (uint32_t)(qi / R) & 1, scr.err, DEVERR_GEMV_FULL);
+      uint2 cd[8];
+      unsigned short sc[8];
+      const unsigned char *rq = raw + rs * Geo::RawBytes;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int row = 16 * warp + 2 * i + rp;
+        cd[i] = ok ? *reinterpret_cast<const uint2 *>(rq + row * 128 + 8 * c) : make_uint2(0u, 0u);
+        sc[i] = ok ? *reinterpret_cast<const unsigned short *>(rq + kTcQ8CodeBytes + row * 16 + 2 * sq) : 0;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[rs]);  // the quad is in registers: its slot may be refilled
+      if (qi >= SA) ok = ok && mbar_wait(&aempty[as], (uint32_t)(qi / SA - 1) & 1, scr.err, DEVERR_GEMV_EMPTY);
+      if (ok) {
+        unsigned char *st = aring + as * kTcAQuad + (c >> 3) * (kTcRows * 128);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int row = 16 * warp + 2 * i + rp;
+          *reinterpret_cast<uint4 *>(st + row * 128 + (((c & 7) ^ (row & 7)) * 16)) =
+              dq8(cd[i], __half2half2(__ushort_as_half(sc[i])));
+        }
+      }
+      fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[as]);
+    }
+  } else if (warp < kTcProducerWarps) {
     // ================= producers: warp w dequantises strip w, one quad per iteration =================
     // lane -> (row rr of the strip, lane-word pair tp): a quarter-warp holds 8 consecutive rows of
     // one pair, so its 16-byte stores into the swizzled rows hit 8 different chunk positions
@@ -179,7 +235,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint4 U0 = make_uint4(0u, 0u, 0u, 0u), U1 = U0;  // lane-words 2tp, 2tp+1 of blocks 0..3
       uint2 D = make_uint2(0u, 0u);                     // the four block scales
       if (ok && valid) {
-        const unsigned char *qb = raw + rs * kTcRawBytes + warp * kQ4QuadBytes;
+        const unsigned char *qb = raw + rs * Geo::RawBytes + warp * kQ4QuadBytes;
         U0 = *reinterpret_cast<const uint4 *>(qb + (rr * 4 + 2 * tp) * 16);
         U1 = *reinterpret_cast<const uint4 *>(qb + (rr * 4 + 2 * tp + 1) * 16);
         D = *reinterpret_cast<const uint2 *>(qb + kQ4QuadCodeBytes + rr * 8);
@@ -242,9 +298,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int qi = 0; qi < nquads; ++qi) {
         const int rs = qi % R;
         if (qi >= R) ok = ok && mbar_wait(&rempty[rs], (uint32_t)(qi / R - 1) & 1, scr.err, DEVERR_GEMV_EMPTY);
-        if (ok) {  // strips past N read as zero
-          mbar_arrive_expect_tx(&rfull[rs], (uint32_t)kTcRawBytes);
-          tma_load_3d(raw + rs * kTcRawBytes, &tmw, 0, q0 + qi, (int32_t)strip0, &rfull[rs], pol_w);
+        if (ok) {  // strips (rows) past N and codes past K read as zero
+          mbar_arrive_expect_tx(&rfull[rs], (uint32_t)Geo::RawBytes);
+          if (Geo::Q8) {
+            tma_load_2d(raw + rs * Geo::RawBytes, &tmw, 128 * (q0 + qi), tile_n * kTcRows, &rfull[rs], pol_w);
+            tma_load_2d(raw + rs * Geo::RawBytes + kTcQ8CodeBytes, &tms, 8 * ((q0 + qi) >> 1), tile_n * kTcRows,
+                        &rfull[rs], pol_w);
+          } else {
+            tma_load_3d(raw + rs * Geo::RawBytes, &tmw, 0, q0 + qi, (int32_t)strip0, &rfull[rs], pol_w);
+          }
           issued = qi + 1;
         } else {
           mbar_arrive(&rfull[rs]);
@@ -347,12 +409,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-template <int NT>
+template <int NT, int QT>
 void launch_tc_t(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, const GemvScratch &sc,
                  int num_sms, cudaStream_t s) {
-  using Geo = TcGeo<NT>;
+  using Geo = TcGeo<NT, QT>;
   const int tiles_n = (int)ceil_div(w.N, kTcRows), tiles_m = (int)ceil_div(M, NT);
-  const int nq = (int)w.row_words;  // K split in whole quads, at least 4 per split
+  const int nq = Geo::Q8 ? (int)ceil_div(w.K, 128) : (int)w.row_words;  // K split in whole quads, >= 4 per split
   int splits = 1;
   const int tiles = tiles_n * tiles_m;
   // split K to minimise waves x (quads per CTA + a fixed per-CTA cost of about 4 quads: TMEM
@@ -393,16 +455,27 @@ void launch_tc_t(const QMat &w, const float *x, int M, int64_t ldx, const Epilog
   const CUtensorMap tmx = make_tmap_3d(sc.xh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kTcK, (uint64_t)M,
                                        (uint64_t)(Kp / kTcK), (uint64_t)Kp * 2, kTcK * 2, kTcK, NT, 2,
                                        CU_TENSOR_MAP_SWIZZLE_128B);
-  // A operand source: the Q4_0 strips as [strip][quad][1152 bytes], read one quad of 8 strips per box
-  const CUtensorMap tmw = make_tmap_3d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, kQ4QuadBytes / 8, (uint64_t)nq,
-                                       (uint64_t)q4_strips(w.N), kQ4QuadBytes, (uint64_t)nq * kQ4QuadBytes,
-                                       kQ4QuadBytes / 8, 1, kTcRows / kQ4StripRows);
+  // A operand source.  Q4_0: the strips as [strip][quad][1152 bytes], one quad of 8 strips per box.
+  // Q8_0: the codes [N][K] (boxes of 128 rows x 128 codes) and the scales [N][ldd] fp16 (boxes of
+  // 128 rows x 8 scales, two quads)
+  CUtensorMap tmw, tms;
+  if (Geo::Q8) {
+    tmw = make_tmap_2d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)w.N, (uint64_t)w.row_words * 4,
+                       (uint64_t)w.row_words * 4, kTcRows, 128);
+    tms = make_tmap_2d(w.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)w.N, (uint64_t)w.ldd, (uint64_t)w.ldd * 2,
+                       kTcRows, 8);
+  } else {
+    tmw = make_tmap_3d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, kQ4QuadBytes / 8, (uint64_t)nq,
+                       (uint64_t)q4_strips(w.N), kQ4QuadBytes, (uint64_t)nq * kQ4QuadBytes, kQ4QuadBytes / 8, 1,
+                       kTcRows / kQ4StripRows);
+    tms = tmw;
+  }
   const size_t smem = Geo::Smem;
   static unsigned long long attr_set = 0;
   int dev = 0;
   FG_CUDA(cudaGetDevice(&dev));
   if (!(attr_set & (1ull << dev))) {
-    FG_CUDA(cudaFuncSetAttribute(k_qgemm_tc<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    FG_CUDA(cudaFuncSetAttribute(k_qgemm_tc<NT, QT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set |= 1ull << dev;
   }
   cudaLaunchConfig_t cfg = {};
@@ -415,13 +488,13 @@ void launch_tc_t(const QMat &w, const float *x, int M, int64_t ldx, const Epilog
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  FG_CUDA(cudaLaunchKernelEx(&cfg, k_qgemm_tc<NT>, tmx, tmw, w, M, ep, sc, splits));
+  FG_CUDA(cudaLaunchKernelEx(&cfg, k_qgemm_tc<NT, QT>, tmx, tmw, tms, w, M, ep, sc, splits));
 }
 
 }  // namespace
 
 bool qgemm_tc_supported(const QMat &w, int M) {
-  return w.qtype == FG_Q4_0 && M >= 1 && w.K % 32 == 0 && w.K >= 32 && w.N >= 1;
+  return (w.qtype == FG_Q4_0 || w.qtype == FG_Q8_0) && M >= 1 && w.K % 32 == 0 && w.K >= 32 && w.N >= 1;
 }
 
 void launch_qgemm_tc(const QMat &w, const float *x, int M, int64_t ldx, const Epilogue &ep, const GemvScratch &sc,
@@ -429,17 +502,28 @@ void launch_qgemm_tc(const QMat &w, const float *x, int M, int64_t ldx, const Ep
   FG_REQUIRE(qgemm_tc_supported(w, M), FG_ERR_SHAPE, "tensor-core GEMM: unsupported matrix");
   FG_REQUIRE(ldx % 4 == 0 && ((uintptr_t)x & 15) == 0, FG_ERR_VALIDATION, "GEMM: x must be 16-byte aligned rows");
   if (M == 0 || w.N == 0) return;
-  // token tile: the smallest UMMA N that covers M, up to 256 tokens per CTA
-  if (M <= 16)
-    launch_tc_t<16>(w, x, M, ldx, ep, sc, num_sms, s);
-  else if (M <= 32)
-    launch_tc_t<32>(w, x, M, ldx, ep, sc, num_sms, s);
-  else if (M <= 64)
-    launch_tc_t<64>(w, x, M, ldx, ep, sc, num_sms, s);
-  else if (M <= 128)
-    launch_tc_t<128>(w, x, M, ldx, ep, sc, num_sms, s);
-  else
-    launch_tc_t<256>(w, x, M, ldx, ep, sc, num_sms, s);
+  // token tile: the smallest UMMA N that covers M, up to 256 tokens per CTA (128 for Q8_0, whose raw
+  // quads are twice as large)
+  if (w.qtype == FG_Q8_0) {
+    if (M <= 16)
+      launch_tc_t<16, FG_Q8_0>(w, x, M, ldx, ep, sc, num_sms, s);
+    else if (M <= 32)
+      launch_tc_t<32, FG_Q8_0>(w, x, M, ldx, ep, sc, num_sms, s);
+    else if (M <= 64)
+      launch_tc_t<64, FG_Q8_0>(w, x, M, ldx, ep, sc, num_sms, s);
+    else
+      launch_tc_t<128, FG_Q8_0>(w, x, M, ldx, ep, sc, num_sms, s);
+  } else if (M <= 16) {
+    launch_tc_t<16, FG_Q4_0>(w, x, M, ldx, ep, sc, num_sms, s);
+  } else if (M <= 32) {
+    launch_tc_t<32, FG_Q4_0>(w, x, M, ldx, ep, sc, num_sms, s);
+  } else if (M <= 64) {
+    launch_tc_t<64, FG_Q4_0>(w, x, M, ldx, ep, sc, num_sms, s);
+  } else if (M <= 128) {
+    launch_tc_t<128, FG_Q4_0>(w, x, M, ldx, ep, sc, num_sms, s);
+  } else {
+    launch_tc_t<256, FG_Q4_0>(w, x, M, ldx, ep, sc, num_sms, s);
+  }
 }
 
 }  // namespace fg

@@ -33,6 +33,24 @@ def test_q4_0_llama_shapes(ctx, N, K, M):
     assert max_rel_err(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("N,K", [(11008, 4096), (4096, 11008)])
+@pytest.mark.parametrize("M", [8, 32, 128, 200])
+def test_q8_0_gemm_llama_shapes(ctx, N, K, M):
+    """Q8_0 on the tensor-core GEMM (fp16 q * d in shared memory, fp32 accumulation in TMEM): batch 8, 32,
+    128 and 200 (two 128-token tiles)."""
+    y, ref = run(ctx, O.Q8_0, "Q8_0", N, K, M, 2000 + M)
+    assert max_rel_err(y, ref) <= TOL
+
+
+@pytest.mark.parametrize("N,K,M", [(66, 1056, 9), (300, 160, 40), (130, 2080, 130), (1, 32, 5)])
+def test_q8_0_gemm_ragged(ctx, N, K, M):
+    """Q8_0 GEMM with K not a multiple of 128 (the last quad's codes and scales read as zero past K),
+    N not a multiple of 128 and token tiles cut short."""
+    y, ref = run(ctx, O.Q8_0, "Q8_0", N, K, M, 3 * N + K + M)
+    assert y.shape == (M, N)
+    assert max_rel_err(y, ref) <= TOL
+
+
 @pytest.mark.parametrize("qt,name", [(O.Q4_0, "Q4_0"), (O.Q8_0, "Q8_0")])
 @pytest.mark.parametrize("N,K,M", [(1, 32, 1), (3, 64, 2), (5, 96, 3), (66, 1056, 4), (130, 2048, 5),
                                    (2, 32, 17), (1000, 512, 1), (32000, 2048, 1)])
