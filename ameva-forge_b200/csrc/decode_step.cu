@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   const int P = kStepGroups * gridDim.x;
   unsigned char *rings = base;                                            // [2][stages][18 KB]
   unsigned char *xarea = base + kStepGroups * kStepStages * kQ4TileBytes;  // staged x / attention scratch
-  float *reds = reinterpret_cast<float *>(xarea + A.xarea_bytes);         // [2][128]
+  float *reds = reinterpret_cast<float *>(xarea + A.xarea_bytes);         // [2 groups][2 buffers][128]
   const int npos = A.pos[0];                                              // keys already in the cache
   const unsigned long long epoch = *reinterpret_cast<volatile unsigned long long *>(A.bar + 1);
   // arrivals every head's attention counter received in earlier launches (each launch adds L S)
@@ -628,7 +628,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   const int gbar = 1 + grp;
   unsigned char *ring = rings + grp * kStepStages * kQ4TileBytes;
   uint64_t *fl = full[grp], *em = empty[grp];
-  float *red = reds + grp * kGroupWarps * kQ4StripRows;
+  float *red = reds + grp * 2 * kGroupWarps * kQ4StripRows;
   int i = 0;  // ring stages consumed
 
   for (int p = 0; p < nphase; ++p) {
@@ -834,10 +834,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
           __syncwarp();
           if (lane == 0) mbar_arrive(&em[sl]);
         }
-        q4_group_red<1>(red, acc, gw, lane);
+        // two partial buffers in turn: a warp refills this one two strips later, after the next
+        // strip's barrier, which the finishing threads reach only once they have read it
+        float *rb = red + ((u - sc.u0) & 1) * (kGroupWarps * kQ4StripRows);
+        q4_group_red<1>(rb, acc, gw, lane);
         named_sync_id(gbar, kGroupThreads);
-        if (ok) finish_strip<1, TP>(w, ep, u, red, &s_inv, gtid, kGroupThreads);
-        named_sync_id(gbar, kGroupThreads);
+        if (ok) finish_strip<1, TP>(w, ep, u, rb, &s_inv, gtid, kGroupThreads);
       }
     }
     // ---------------- end of phase: grid barrier
@@ -942,7 +944,7 @@ size_t decode_step_xarea(int d, int G, int64_t H, int64_t I, int64_t qdim) {
 
 size_t decode_step_smem(int d, int G, int64_t H, int64_t I, int64_t qdim) {
   return 128 + (size_t)kStepGroups * kStepStages * kQ4TileBytes + decode_step_xarea(d, G, H, I, qdim) +
-         (size_t)kStepGroups * kGroupWarps * kQ4StripRows * 4;
+         (size_t)kStepGroups * 2 * kGroupWarps * kQ4StripRows * 4;
 }
 
 int decode_step_vctas(int num_sms) { return kStepGroups * num_sms; }

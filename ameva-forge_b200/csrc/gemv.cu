@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kThreads, 2)
   const Sched sc = make_sched(w.N, kQ4StripRows, 1, blockIdx.x, gridDim.x);  // units = strips
   Q4X<MV> X;
   X.carve(ring + kQ4Stages * kQ4TileBytes, nb, nq * 4);
-  float *red = reinterpret_cast<float *>(ring + kQ4Stages * kQ4TileBytes + Q4X<MV>::bytes(X.nbx));  // [8][16][MV]
+  float *red = reinterpret_cast<float *>(ring + kQ4Stages * kQ4TileBytes + Q4X<MV>::bytes(X.nbx));  // [2][8][16][MV]
 
   if (tid == 0) {
     for (int s = 0; s < kQ4Stages; ++s) {
@@ -142,10 +142,12 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
     }
-    q4_group_red<MV>(red, acc, warp, lane);
+    // two partial buffers in turn: a warp refills this one two strips later, after the next strip's
+    // barrier, which the finishing threads reach only once they have read it
+    float *rb = red + ((u - sc.u0) & 1) * (kGroupWarps * kQ4StripRows * MV);
+    q4_group_red<MV>(rb, acc, warp, lane);
     named_sync(kCThreads);
-    if (ok) finish_strip<MV>(w, ep, u, red, s_inv, tid, kCThreads);
-    named_sync(kCThreads);
+    if (ok) finish_strip<MV>(w, ep, u, rb, s_inv, tid, kCThreads);
   }
 }
 
@@ -330,7 +332,7 @@ size_t q4_smem(int64_t K, int MV, int stages = 4) {
     case 3: xbytes = Q4X<3>::bytes(nbx); break;
     default: xbytes = Q4X<4>::bytes(nbx); break;
   }
-  return 128 + (size_t)stages * kQ4TileBytes + xbytes + (size_t)kGroupWarps * kQ4StripRows * MV * 4;
+  return 128 + (size_t)stages * kQ4TileBytes + xbytes + (size_t)2 * kGroupWarps * kQ4StripRows * MV * 4;
 }
 size_t q8_smem(int64_t K, int MV) {
   return 128 + (size_t)kStages * Geo<kRows, kTileBytes, 16>::SB + (size_t)MV * K * 4 + (size_t)kRows * MV * 4;
