@@ -126,10 +126,10 @@ __global__ void k_x_to_f16(const float *__restrict__ x, int64_t ldx, int M, int6
   }
 }
 
-// Q8_0: eight int8 codes -> four fp16 pairs q * d: 0x6400 | (code ^ 0x80) is 1024 + q + 128 exactly,
-// one exact subtraction leaves q, one multiply by d rounds once.
+// Q8_0: eight device codes (q + 128, unsigned) -> four fp16 pairs q * d: 0x6400 | (q + 128) is
+// 1024 + q + 128 exactly, one exact subtraction leaves q, one multiply by d rounds once.
 __device__ __forceinline__ uint4 dq8(uint2 c, __half2 d2) {
-  const uint32_t u0 = c.x ^ 0x80808080u, u1 = c.y ^ 0x80808080u;
+  const uint32_t u0 = c.x, u1 = c.y;
   const uint32_t h[4] = {__byte_perm(u0, 0x64646464u, 0x4140), __byte_perm(u0, 0x64646464u, 0x4342),
                          __byte_perm(u1, 0x64646464u, 0x4140), __byte_perm(u1, 0x64646464u, 0x4342)};
   const __half2 off = __float2half2_rn(1152.0f);
@@ -212,11 +212,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (qi >= SA) ok = ok && mbar_wait(&aempty[as], (uint32_t)(qi / SA - 1) & 1, scr.err, DEVERR_GEMV_EMPTY);
       if (ok) {
         unsigned char *st = aring + as * kTcAQuad + (c >> 3) * (kTcRows * 128);
+        // columns past K are zero (the scale plane's padding past K / 32 blocks is not)
+        const bool kin = (int64_t)(q0 + qi) * 128 + 8 * c < w.K;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int row = 16 * warp + 2 * i + rp;
           *reinterpret_cast<uint4 *>(st + row * 128 + (((c & 7) ^ (row & 7)) * 16)) =
-              dq8(cd[i], __half2half2(__ushort_as_half(sc[i])));
+              kin ? dq8(cd[i], __half2half2(__ushort_as_half(sc[i]))) : make_uint4(0u, 0u, 0u, 0u);
         }
       }
       fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy

@@ -27,14 +27,6 @@
 // d * 2^-e * D' into an fp32 accumulator.  Scales are local to a block, so
 // one large activation does not coarsen the others.  The RMSNorm's 1/rms
 // multiplies the finished sums.
-//
-// One token (MV = 1) has no second token for B columns 4-7, so it splits the
-// block's elements over the columns instead ("column split"): the high
-// nibbles enter the MMA as 16 q (one AND, no shift), columns 0-3 carry the
-// digits of elements 0-15 (zero for 16-31) and columns 4-7 those of elements
-// 16-31 (zero for 0-15), with accumulator inputs -8 and -128 times the digit
-// sums of the respective half.  Every lane's result is then a useful partial
-// sum; the halves combine exactly at the end as lo + hi / 16.
 #pragma once
 #include "epilogue.cuh"
 #include "tma.cuh"
@@ -159,49 +151,24 @@ __device__ __forceinline__ void finish_group(const QMat &w, const Epilogue &ep, 
 template <int MV>
 struct Q4X {
   static constexpr int NM = (MV + 1) / 2;  // MMAs per block: two tokens each
-  static constexpr int CXR = MV == 1 ? 4 : 2 * MV;  // accumulator-input rows: lane kinds t (MV = 1) or (token, t & 1)
   uint2 *xb;    // [nbx][3 MV digit columns][4 lane-words t] digit pairs (k 4t.., 16+4t..)
-  int *cx0;     // [CXR][nbx] MMA C of the lane kind, column 2t
-  int *cx1;     // [CXR][nbx] column 2t+1
+  int *cx0;     // [2 MV][nbx] MMA C of lane kind (token, t & 1), column 2t
+  int *cx1;     // [2 MV][nbx] column 2t+1
   float *fbk;   // [MV][nbx] block factors 2^-e
   int nb, nbx;  // blocks of K, blocks staged (a multiple of 4; zero past nb)
 
   __host__ __device__ static size_t bytes(int nbx) {
-    return (size_t)nbx * 3 * MV * 32 + (size_t)2 * CXR * nbx * 4 + (size_t)MV * nbx * 4;
+    return (size_t)nbx * 3 * MV * 32 + (size_t)4 * MV * nbx * 4 + (size_t)MV * nbx * 4;
   }
   __device__ void carve(unsigned char *base, int nb_, int nbx_) {
     nb = nb_;
     nbx = nbx_;
     xb = reinterpret_cast<uint2 *>(base);
     cx0 = reinterpret_cast<int *>(xb + nbx * 3 * MV * 4);
-    cx1 = cx0 + CXR * nbx;
-    fbk = reinterpret_cast<float *>(cx1 + CXR * nbx);
+    cx1 = cx0 + 2 * MV * nbx;
+    fbk = reinterpret_cast<float *>(cx1 + 2 * MV * nbx);
   }
 };
-
-// Accumulator inputs and block factor of block bb for one token (MV = 1, column split), written by
-// the 8 staging lanes of the block after the digit sums of each half are reduced (lanes q < 4 hold
-// elements 0-15, lanes q >= 4 elements 16-31).
-__device__ __forceinline__ void q4_store_c1(const Q4X<1> &X, int bb, int q, int shi, int smi, int slo, float fb) {
-#pragma unroll
-  for (int o = 1; o < 4; o <<= 1) {
-    shi += __shfl_xor_sync(0xffffffffu, shi, o);
-    smi += __shfl_xor_sync(0xffffffffu, smi, o);
-    slo += __shfl_xor_sync(0xffffffffu, slo, o);
-  }
-  if (q == 0) {  // lane kinds t = 0 (hi, mid) and t = 1 (lo, 0) of elements 0-15
-    X.cx0[bb] = -8 * shi;
-    X.cx1[bb] = -8 * smi;
-    X.cx0[X.nbx + bb] = -8 * slo;
-    X.cx1[X.nbx + bb] = 0;
-    X.fbk[bb] = fb;
-  } else if (q == 4) {  // t = 2, 3 of elements 16-31, whose codes enter as 16 q
-    X.cx0[2 * X.nbx + bb] = -128 * shi;
-    X.cx1[2 * X.nbx + bb] = -128 * smi;
-    X.cx0[3 * X.nbx + bb] = -128 * slo;
-    X.cx1[3 * X.nbx + bb] = 0;
-  }
-}
 
 // Digits of 4 consecutive elements packed as s8 bytes.
 __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
@@ -260,25 +227,21 @@ __device__ __forceinline__ void q4_stage_x(const Q4X<MV> &X, const float *x, int
       col[0] = pack_s8x4(hi[0], hi[1], hi[2], hi[3]);
       col[8] = pack_s8x4(mi[0], mi[1], mi[2], mi[3]);
       col[16] = pack_s8x4(lo[0], lo[1], lo[2], lo[3]);
-      // non-finite inputs make the block factor NaN, so the outputs are NaN
-      const float fb = amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000);
-      if constexpr (MV == 1) {
-        q4_store_c1(X, bb, q, shi, smi, slo, fb);
-      } else {
 #pragma unroll
-        for (int o = 1; o < 8; o <<= 1) {
-          shi += __shfl_xor_sync(0xffffffffu, shi, o);
-          smi += __shfl_xor_sync(0xffffffffu, smi, o);
-          slo += __shfl_xor_sync(0xffffffffu, slo, o);
-        }
-        if (q == 0) {
-          // C of the lanes holding (hi, mid) and (lo, 0) of token m
-          X.cx0[(2 * m) * X.nbx + bb] = -8 * shi;
-          X.cx1[(2 * m) * X.nbx + bb] = -8 * smi;
-          X.cx0[(2 * m + 1) * X.nbx + bb] = -8 * slo;
-          X.cx1[(2 * m + 1) * X.nbx + bb] = 0;
-          X.fbk[m * X.nbx + bb] = fb;
-        }
+      for (int o = 1; o < 8; o <<= 1) {
+        shi += __shfl_xor_sync(0xffffffffu, shi, o);
+        smi += __shfl_xor_sync(0xffffffffu, smi, o);
+        slo += __shfl_xor_sync(0xffffffffu, slo, o);
+      }
+      if (q == 0) {
+        // C of the lanes holding (hi, mid) and (lo, 0) of token m
+        X.cx0[(2 * m) * X.nbx + bb] = -8 * shi;
+        X.cx1[(2 * m) * X.nbx + bb] = -8 * smi;
+        X.cx0[(2 * m + 1) * X.nbx + bb] = -8 * slo;
+        X.cx1[(2 * m + 1) * X.nbx + bb] = 0;
+        // non-finite inputs make the block factor NaN, so the outputs are NaN
+        X.fbk[m * X.nbx + bb] =
+            amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000);
       }
     }
     ss = warp_sum(ss);
@@ -343,8 +306,19 @@ static __device__ __forceinline__ void q4_stage_x_fold(const Q4X<1> &X, const fl
     col[0] = pack_s8x4(hi[0], hi[1], hi[2], hi[3]);
     col[8] = pack_s8x4(mi[0], mi[1], mi[2], mi[3]);
     col[16] = pack_s8x4(lo[0], lo[1], lo[2], lo[3]);
-    q4_store_c1(X, bb, q, shi, smi, slo,
-                amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      shi += __shfl_xor_sync(0xffffffffu, shi, o);
+      smi += __shfl_xor_sync(0xffffffffu, smi, o);
+      slo += __shfl_xor_sync(0xffffffffu, slo, o);
+    }
+    if (q == 0) {
+      X.cx0[bb] = -8 * shi;
+      X.cx1[bb] = -8 * smi;
+      X.cx0[X.nbx + bb] = -8 * slo;
+      X.cx1[X.nbx + bb] = 0;
+      X.fbk[bb] = amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000);
+    }
   }
   ss = warp_sum(ss);
   if (lane == 0) ss_out[warp] = ss;
@@ -366,22 +340,10 @@ struct Q4Lane {
   bool xv[NM];
   const int *c0l[NM], *c1l[NM];
   const float *fbl[NM];
-  const uint32_t *xw;  // MV = 1: this lane's digit word of block 0 (24 words per block)
-  bool xhigh;          // MV = 1: B column of elements 16-31 (b1) rather than 0-15 (b0)
   __device__ void init(const Q4X<MV> &X, int lane) {
     const int gq = lane >> 2, t = lane & 3;
     a_off = (gq * 4 + t) * 16;
     d_off = kQ4QuadCodeBytes + gq * 8;
-    if constexpr (MV == 1) {  // column split: B column gq = digit gq & 3 of half gq >> 2; digit 3 is zero
-      xv[0] = (gq & 3) < 3;
-      xhigh = gq >= 4;
-      xw = reinterpret_cast<const uint32_t *>(X.xb) + ((xv[0] ? (gq & 3) : 0) * 4 + t) * 2 + (xhigh ? 1 : 0);
-      xl[0] = nullptr;
-      c0l[0] = X.cx0 + t * X.nbx;
-      c1l[0] = X.cx1 + t * X.nbx;
-      fbl[0] = X.fbk;
-      return;
-    }
     // B column gq of MMA i = digit (gq & 3) of token 2i + (gq >> 2); digit 3 is the zero column
 #pragma unroll
     for (int im = 0; im < NM; ++im) {
@@ -417,20 +379,12 @@ __device__ __forceinline__ void q4_quad(const unsigned char *qb, int Q, const Q4
     const float fbv[4] = {FB.x, FB.y, FB.z, FB.w};
 #pragma unroll
     for (int bi = 0; bi < 4; ++bi) {
+      uint2 B = make_uint2(0u, 0u);
+      if (L.xv[im]) B = L.xl[im][(bb0 + bi) * 3 * MV * 4];
       const uint32_t wa = a0w[bi], wb = a1w[bi];
       int di[4];
-      if constexpr (MV == 1) {  // column split: high nibbles as 16 q, B on its half only
-        uint32_t w = 0u;
-        if (L.xv[0]) w = L.xw[(bb0 + bi) * 24];
-        const uint32_t b0 = L.xhigh ? 0u : w, b1 = L.xhigh ? w : 0u;
-        imma_u8s8(di, wa & 0x0F0F0F0Fu, wb & 0x0F0F0F0Fu, wa & 0xF0F0F0F0u, wb & 0xF0F0F0F0u, b0, b1, c0v[bi],
-                  c1v[bi]);
-      } else {
-        uint2 B = make_uint2(0u, 0u);
-        if (L.xv[im]) B = L.xl[im][(bb0 + bi) * 3 * MV * 4];
-        imma_u8s8(di, wa & 0x0F0F0F0Fu, wb & 0x0F0F0F0Fu, (wa >> 4) & 0x0F0F0F0Fu, (wb >> 4) & 0x0F0F0F0Fu, B.x,
-                  B.y, c0v[bi], c1v[bi]);
-      }
+      imma_u8s8(di, wa & 0x0F0F0F0Fu, wb & 0x0F0F0F0Fu, (wa >> 4) & 0x0F0F0F0Fu, (wb >> 4) & 0x0F0F0F0Fu, B.x, B.y,
+                c0v[bi], c1v[bi]);
       const float2 v = make_float2((float)(di[0] * 128 + di[1]), (float)(di[2] * 128 + di[3]));
       // scale pair (row g, row g+8) of block bi: halves bi of D0 and D1
       const uint32_t dpair = __byte_perm(bi < 2 ? D0.x : D0.y, bi < 2 ? D1.x : D1.y, (bi & 1) ? 0x7632 : 0x5410);
@@ -458,18 +412,6 @@ __device__ __forceinline__ void q4_tile(const unsigned char *st, int Q0, int nqt
 template <int MV>
 __device__ __forceinline__ void q4_group_red(float *red, float2 (&acc)[Q4X<MV>::NM], int warp, int lane) {
   const int gq = lane >> 2, t = lane & 3;
-  if constexpr (MV == 1) {  // column split: (t0, t1) hold elements 0-15, (t2, t3) elements 16-31 times 16
-    const float bx = __shfl_down_sync(0xffffffffu, acc[0].x, 1);
-    const float by = __shfl_down_sync(0xffffffffu, acc[0].y, 1);
-    const float px = acc[0].x * 128.0f + bx * 0.0078125f, py = acc[0].y * 128.0f + by * 0.0078125f;
-    const float qx = __shfl_down_sync(0xffffffffu, px, 2), qy = __shfl_down_sync(0xffffffffu, py, 2);
-    if (t == 0) {
-      red[16 * warp + gq] = px + qx * 0.0625f;
-      red[16 * warp + gq + 8] = py + qy * 0.0625f;
-    }
-    acc[0] = make_float2(0.0f, 0.0f);
-    return;
-  }
 #pragma unroll
   for (int im = 0; im < Q4X<MV>::NM; ++im) {
     // lanes t even hold 128 D_hi + D_mid sums, lane t + 1 the 128 D_lo sums

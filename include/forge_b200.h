@@ -187,8 +187,9 @@ int fg_flash_attention(fg_ctx *ctx, fg_handle q, fg_handle k, fg_handle v, float
  * and q and out 4-byte aligned; other pointers give FG_ERR_VALIDATION.
  * Runs on `stream`
  * (a cudaStream_t; NULL = legacy default stream) of the current device.
- * Split-KV scratch comes from a 2 MiB static device array: shapes that need
- * more return FG_ERR_VALIDATION.  Calls on one device must not overlap in
+ * Split-KV scratch comes from a 2 MiB static device array: shapes whose
+ * partials would need more run with fewer splits (one split needs none).
+ * Calls on one device must not overlap in
  * time (they share the array); calls queued on one stream are safe.  The
  * first call on each device looks up the array's address and must not be
  * made during stream capture. */
