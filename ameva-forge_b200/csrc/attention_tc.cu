@@ -17,14 +17,17 @@
 //    and O_t += P_t V (N = head_dim, K = 128 keys, V read MN-major) into
 //    columns [256 + 128 t, ...), with P_t read from TMEM (the A operand) where
 //    the softmax wrote it over the first 64 columns of S_t.  S_t of the next
-//    block is issued once P_t V has completed;
+//    block is issued right after P_t V: the tensor core runs one thread's MMAs
+//    in issue order, so it lands after P_t V has read P_t.  The issuing thread
+//    polls for P with a short suspend time, to start the MMAs soon after the
+//    softmax warps arrive;
 //  * each tile has a softmax warpgroup, one thread per query row = TMEM lane:
 //    it reads the row of S (tcgen05.ld), applies the scale and the
 //    causal/extent mask, updates the running max m and sum l (exp2 domain), and
 //    writes P as fp16 pairs (tcgen05.st).  m moves only when a row's maximum
 //    grows by more than 2^8 (P then stays <= 256, exact in fp16 range); only
-//    then is the O row rescaled in TMEM (no MMA touches O_t during the tile's
-//    softmax);
+//    then is the O row rescaled in TMEM (P_t V of the previous block completed
+//    before this block's scores did);
 //  * the same threads finish with out = O / max(l, 1e-12) in fp32.
 // Every wait is bounded (tma.cuh); on a timeout the device error word is set
 // and the CTA skips its stores, drains its copies and frees its TMEM.
@@ -319,7 +322,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
         for (int t = 0; t < kFaTiles; ++t) {
           if (j >= nb[t]) continue;
-          ok = ok && mbar_wait(&pfull[t], (uint32_t)j & 1, a.err, DEVERR_ATTN_FULL);
+          ok = ok && mbar_wait_poll(&pfull[t], (uint32_t)j & 1, a.err, DEVERR_ATTN_FULL);
           if (!vin) {
             ok = ok && mbar_wait(&vfull[j & 1], (uint32_t)(j >> 1) & 1, a.err, DEVERR_ATTN_FULL);
             vin = true;
@@ -332,8 +335,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
               ok = ok && mbar_wait(&kfull[(j + 1) & 1], (uint32_t)((j + 1) >> 1) & 1, a.err, DEVERR_ATTN_FULL);
               kin = true;
             }
-            // S_t of the next block overwrites P_t: wait until P_t V has read it
-            ok = ok && mbar_wait(&pvdone[t], (uint32_t)j & 1, a.err, DEVERR_ATTN_EMPTY);
+            // S_t of the next block overwrites P_t; issued after P_t V by this thread, the tensor core
+            // runs it after P_t V has read P_t
             tc_fence_after();
             issue_s(t, j + 1);
           }

@@ -59,6 +59,33 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *e
   }
 }
 
+// try_wait that suspends for at most ~100 ns: for a single thread whose wake-up
+// latency is on the critical path (the hardware may resume a long-suspended
+// thread hundreds of cycles after the phase completes).
+__device__ __forceinline__ bool mbar_try_wait_short(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(100u)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait with short suspends; the same bounds.
+__device__ __forceinline__ bool mbar_wait_poll(uint64_t *bar, uint32_t parity, int *err, int code) {
+  if (mbar_try_wait_short(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait_short(bar, parity)) return true;
+    if (err && *(volatile int *)err != 0) return false;  // another CTA already failed: stop early
+    if (global_ns() - t0 > kWaitTimeoutNs) {
+      if (err) atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
 // Wait for a phase during a drain: bounded by time only (a drain must wait
 // for copies in flight even after another thread reported an error).
 __device__ __forceinline__ void mbar_wait_drain(uint64_t *bar, uint32_t parity) {
