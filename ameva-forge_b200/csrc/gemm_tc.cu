@@ -1,36 +1,35 @@
-// Q4_0 GEMM on the 5th-generation tensor cores (tcgen05, sm_100a):
+// Q4_0 / Q8_0 GEMM on the 5th-generation tensor cores (tcgen05, sm_100a):
 //   Y[m, n] = sum_k X[m, k] W[n, k]   (+ the fused epilogues of epilogue.cuh)
 // for more than 4 token rows (prefill chunks, batched decode).
 //
-// The weight matrix is the UMMA A operand: a CTA owns 128 weight rows (8 of
-// the 16-row strips of the Q4_0 layout, common.cuh) and NT tokens (16..256,
-// the UMMA N), so D = W_tile X_tile^T sits in TMEM as 128 lanes x NT fp32
-// columns.  K advances by quads (128 columns = two 64-wide swizzle atoms),
-// through three shared-memory rings:
-//  * raw: one thread copies the quad of the tile's 8 strips (one 3-D TMA box,
-//    9 KB) up to RAW quads ahead;
-//  * A: warp w dequantises strip w into the canonical K-major, 128-byte
-//    swizzled layout (row r at r * 128 bytes, 16-byte chunk c at c ^ (r & 7),
-//    8-row atoms 1024 bytes apart): (q - 8) * d in one rounding (the fp16
-//    pair 1024 + q, one exact add, one multiply), whole 16-byte chunks, no
-//    bank conflicts.  Both operands are fp16: a Q4_0 weight (q - 8) * d
-//    carries 15 significant bits, which fp16 keeps to 2^-12 (bf16 would lose
-//    2^-9 and sit at the GEMM tolerance);
+// The weight matrix is the UMMA A operand and lives in TMEM: a CTA owns 128
+// weight rows (one per TMEM lane) and NT tokens (16..256, the UMMA N), so
+// D = W_tile X_tile^T sits in TMEM as 128 lanes x NT fp32 columns, next to a
+// ring of dequantised A stages of 64 columns (one quad = 128 K columns as fp16
+// pairs).  K advances by quads through
+//  * raw: one thread copies the quad's codes and scales with TMA boxes laid
+//    out [row][16 bytes] (Q4_0: one box per lane-word index of the strip
+//    layout; Q8_0: one box per 16 codes), so that a warp reading one 16-byte
+//    unit for 32 consecutive rows hits every bank once;
+//  * A: producer warp w owns TMEM lanes 32 (w % 4) .. + 31 (= weight rows) and
+//    half w / 4 of the quad's K: each thread dequantises its row's 64 values
+//    ((q - 8) d, resp. q d, in one fp16 rounding) into 32 registers and stores
+//    them with one tcgen05.st;
 //  * B: one thread copies the quad's [2][NT][64] fp16 chunks of X (converted
 //    and zero-padded to whole quads by k_x_to_f16) with the TMA unit's
-//    128-byte swizzle, up to RB quads ahead;
+//    128-byte swizzle;
 //  * one thread of the MMA warp issues eight tcgen05.mma.kind::f16 (K = 16
-//    each) per quad with shared-memory descriptors and commits them to the
-//    A and B slots' "empty" mbarriers; after the last quad it commits to the
-//    "accumulator" mbarrier;
+//    each, A from TMEM, B from shared memory) per quad and commits them to
+//    the A and B stages' "empty" mbarriers; after the last quad it commits to
+//    the "accumulator" mbarrier;
 //  * warps 0-3 (TMEM lanes 0..127) read D with tcgen05.ld into a shared tile
 //    that the stages no longer use, then store it with 16-byte stores and the
 //    epilogue on row pairs (RoPE / SwiGLU partners are neighbouring columns).
-// Work per quad is counted in shared-memory instructions: the MMA thread's
-// waits, MMAs and commits queue behind the producers' stores, so both sides
-// work at quad granularity.  When the (weight tile, token tile) grid is
-// small against the GPU, K is split over several CTAs (the split count that
-// minimises waves x quads per CTA): each
+// Shared memory holds only the raw quads and X, so up to 64 tokens two CTAs
+// share an SM (256 TMEM columns each) and their small-N MMAs overlap: A read
+// from TMEM leaves the shared-memory bandwidth to the copies.  When the
+// (weight tile, token tile) grid is small against the GPU, K is split over
+// several CTAs (the split count that minimises waves x quads per CTA): each
 // writes its partial tile and the last one of a tile to arrive sums them in
 // split order (deterministic) and runs the epilogue.
 //
@@ -46,42 +45,45 @@
 namespace fg {
 namespace {
 
-constexpr int kTcRows = 128;                 // UMMA M: weight rows per CTA
-constexpr int kTcK = 64;                     // K per MMA group (one 128-byte swizzle atom of fp16)
-constexpr int kTcProducerWarps = 8;          // warp w dequantises strip w (warps 0-3 also run the epilogue)
+constexpr int kTcRows = 128;                 // UMMA M: weight rows per CTA = TMEM lanes
+constexpr int kTcK = 64;                     // K per B chunk (one 128-byte swizzle atom of fp16)
+constexpr int kTcProducerWarps = 8;          // warp w: TMEM lanes 32 (w % 4).., K half w / 4 (warps 0-3 also
+                                             // run the epilogue)
 constexpr int kTcMmaWarp = kTcProducerWarps;       // TMEM owner, one thread issues the MMAs
-constexpr int kTcRawWarp = kTcProducerWarps + 1;   // one thread loads the raw Q4_0 quads
+constexpr int kTcRawWarp = kTcProducerWarps + 1;   // one thread loads the raw quads
 constexpr int kTcThreads = (kTcProducerWarps + 3) * 32;  // + one thread that loads the B tiles
-constexpr int kTcAQuad = 2 * kTcRows * kTcK * 2;  // dequantised A per quad: two 16 KB swizzled stages
-constexpr int kTcRawBytes = (kTcRows / kQ4StripRows) * kQ4QuadBytes;  // 8 strips x 1152 bytes
+constexpr int kTcACols = 64;                 // TMEM columns of one dequantised quad (128 fp16 per row)
 constexpr int kTcMaxRing = 16;
+// raw quad: Q4_0 4 x [128 rows][16 B] codes (lane-words t = 0..3 of blocks 0..3) + [128 rows][8 B] scales;
+// Q8_0 8 x [128 rows][16 B] codes (16 codes each) + [128 rows][8 scales] (two quads)
+constexpr int kTcUnitBytes = kTcRows * 16;
+constexpr int kTcQ4RawBytes = 4 * kTcUnitBytes + kTcRows * 8;
+constexpr int kTcQ8RawBytes = 8 * kTcUnitBytes + kTcRows * 16;
 
-// Three rings of whole quads (128 K columns), sized per token tile within 227 KB.
-// A bulk-tensor copy takes 1-2.5 us to land under load, so the copy rings run far ahead:
-//  * B: the quad's two 64-column chunks of X, [2][NT][64] fp16 swizzled (one 3-D box);
-//  * A: the quad's dequantised weights, [2][128][64] fp16 swizzled (producer warps);
-//  * raw: the quad of the tile's 8 strips (9 KB, one 3-D box).
-//  Q8_0 (QT = FG_Q8_0, NT <= 128): the raw quad is the tile's 128 rows x 128 int8 codes (16 KB, one
-//  2-D box) and their 8-scale groups (2 KB, one 2-D box of the scales of two quads).
-constexpr int kTcQ8CodeBytes = kTcRows * 128, kTcQ8RawBytes = kTcQ8CodeBytes + kTcRows * 16;
-
+// Rings sized per token tile: up to NT = 64 two CTAs share an SM (<= 110 KB of shared memory and 256
+// TMEM columns each), NT = 128 and 256 take an SM (512 columns; at NT = 128 two CTAs with two B stages
+// each ran 2.2 times slower).  A bulk-tensor copy takes 1-2.5 us to land
+// under load, so the copy rings run far ahead.
 template <int NT, int QT = FG_Q4_0>
 struct TcGeo {
   static constexpr bool Q8 = QT == FG_Q8_0;
-  static constexpr int RawBytes = Q8 ? kTcQ8RawBytes : kTcRawBytes;
+  static constexpr bool Two = NT <= 64;  // two CTAs per SM
+  static constexpr int RawBytes = Q8 ? kTcQ8RawBytes : kTcQ4RawBytes;
   static constexpr int BQuad = 2 * NT * kTcK * 2;  // B bytes per quad
-  static constexpr int RB = NT <= 16 ? 16 : NT <= 32 ? 8 : NT <= 64 ? 5 : NT <= 128 ? 3 : 2;
-  static constexpr int SA = Q8 ? (NT >= 64 ? 2 : 3) : NT <= 128 ? 3 : 2;
-  static constexpr int RAW = Q8 ? 3 : NT <= 32 ? 6 : NT <= 64 ? 4 : 3;
-  static constexpr int TmemCols = NT < 32 ? 32 : NT;  // allocation: a power of two >= 32
-  static constexpr size_t AOff = (size_t)RB * BQuad;
-  static constexpr size_t RawOff = AOff + (size_t)SA * kTcAQuad;
+  static constexpr int RB = Q8 ? (NT <= 16 ? 8 : NT <= 32 ? 4 : NT <= 64 ? 3 : 3)
+                               : (NT <= 16 ? 8 : NT <= 32 ? 6 : NT <= 64 ? 4 : NT <= 128 ? 3 : 2);
+  static constexpr int RAW = Q8 ? (NT <= 64 ? 3 : 4) : (NT <= 16 ? 6 : NT <= 32 ? 5 : 4);
+  static constexpr int SA = 3;  // dequantised A stages in TMEM
+  static constexpr int TmemCols = Two ? 256 : 512;
+  static constexpr int ACol = TmemCols - SA * kTcACols;  // first column of the A ring (after D)
+  static constexpr size_t RawOff = (size_t)RB * BQuad;
   // + 1 KB for the 1024-byte alignment of the swizzled tiles
   static constexpr size_t Smem = 1024 + RawOff + (size_t)RAW * RawBytes;
+  static_assert(RB <= kTcMaxRing && RAW <= kTcMaxRing, "rings");
+  static_assert(ACol >= NT, "TMEM: accumulator and A ring");
+  static_assert(Smem + 1024 <= (Two ? 113u * 1024 : 232448u), "shared memory per CTA");
+  static_assert(Smem - 1024 >= (size_t)NT * kTcRows * 4, "the epilogue tile reuses the rings");
   static_assert(!Q8 || NT <= 128, "Q8_0 token tiles up to 128");
-  static_assert(RB <= kTcMaxRing && SA <= kTcMaxRing && RAW <= kTcMaxRing && Smem + 1024 <= 232448,
-                "shared memory per CTA");
-  static_assert(RawOff >= (size_t)NT * kTcRows * 4, "the epilogue tile reuses the B and A rings");
 };
 
 // Instruction descriptor: fp16 A and B, fp32 D, both K-major, M = 128, N = NT.
@@ -143,14 +145,14 @@ __device__ __forceinline__ uint4 dq8(uint2 c, __half2 d2) {
 }
 
 template <int NT, int QT>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(kTcThreads, NT <= 64 ? 2 : 1)  // two CTAs per SM up to 64 tokens
     k_qgemm_tc(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                const __grid_constant__ CUtensorMap tms, QMat w, int M, Epilogue ep, GemvScratch scr, int splits) {
   using Geo = TcGeo<NT, QT>;
   extern __shared__ __align__(1024) unsigned char tc_smem_raw[];
   unsigned char *sm = tc_smem_raw + ((1024 - (smem_u32(tc_smem_raw) & 1023)) & 1023);
   constexpr int RB = Geo::RB, SA = Geo::SA, R = Geo::RAW;
-  unsigned char *bring = sm, *aring = sm + Geo::AOff, *raw = sm + Geo::RawOff;
+  unsigned char *bring = sm, *raw = sm + Geo::RawOff;
   __shared__ __align__(8) uint64_t bfull[kTcMaxRing], bempty[kTcMaxRing], afull[kTcMaxRing], aempty[kTcMaxRing];
   __shared__ __align__(8) uint64_t rfull[kTcMaxRing], rempty[kTcMaxRing], accum;
   __shared__ uint32_t s_taddr;
@@ -162,8 +164,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   // this split's quads (128-wide K chunks, zero-padded at the end of a row)
   const int q0 = (int)((int64_t)split * nq / splits), q1 = (int)((int64_t)(split + 1) * nq / splits);
   const int nquads = q1 - q0;
-  const int64_t strip0 = (int64_t)tile_n * (kTcRows / kQ4StripRows);
-  const int nvalid = (int)std::min<int64_t>(kTcRows / kQ4StripRows, q4_strips(w.N) - strip0);  // strips in range
   const int m0 = tile_m * NT;
 
   if (tid == 0) {
@@ -190,86 +190,83 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   bool ok = true;
-  if (Geo::Q8 && warp < kTcProducerWarps) {
-    // ================= Q8_0 producers: warp w dequantises rows 16w .. 16w+15 =================
-    // lane -> (row parity rp, 16-byte output chunk c = 8 codes): 16 lanes read one row's 128 code
-    // bytes and write its two swizzled 128-byte rows; a quad's scale sits at 4 (quad & 1) + c / 4
-    const int rp = lane >> 4, c = lane & 15;
+  if (warp < kTcProducerWarps) {
+    // ============ producers: thread = weight row r = TMEM lane, warp half hb of the quad's K ============
+    const int quad = warp & 3, hb = warp >> 2, r = 32 * quad + lane;
+    // this thread's 32 columns of A stage `as`: lane quadrant of the warp, columns 32 hb ..
+    const uint32_t ta = taddr + ((uint32_t)(32 * quad) << 16) + Geo::ACol + 32 * hb;
     for (int qi = 0; qi < nquads; ++qi) {
-      const int rs = qi % R, as = qi % SA, sq = 4 * ((q0 + qi) & 1) + (c >> 2);
+      const int rs = qi % R, as = qi % SA, Q = q0 + qi;
       ok = ok && mbar_wait(&rfull[rs], (uint32_t)(qi / R) & 1, scr.err, DEVERR_GEMV_FULL);
-      uint2 cd[8];
-      unsigned short sc[8];
       const unsigned char *rq = raw + rs * Geo::RawBytes;
+      uint32_t out[32];
+      if constexpr (Geo::Q8) {
+        // units 4 hb .. 4 hb + 3 of 16 codes (device codes q + 128), block = unit / 2; the quad's four
+        // scales are half (Q & 1) of the row's 8-scale box
+        uint4 c[4];
+        uint32_t sc = 0u;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int row = 16 * warp + 2 * i + rp;
-        cd[i] = ok ? *reinterpret_cast<const uint2 *>(rq + row * 128 + 8 * c) : make_uint2(0u, 0u);
-        sc[i] = ok ? *reinterpret_cast<const unsigned short *>(rq + kTcQ8CodeBytes + row * 16 + 2 * sq) : 0;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rempty[rs]);  // the quad is in registers: its slot may be refilled
-      if (qi >= SA) ok = ok && mbar_wait(&aempty[as], (uint32_t)(qi / SA - 1) & 1, scr.err, DEVERR_GEMV_EMPTY);
-      if (ok) {
-        unsigned char *st = aring + as * kTcAQuad + (c >> 3) * (kTcRows * 128);
-        // columns past K are zero (the scale plane's padding past K / 32 blocks is not)
-        const bool kin = (int64_t)(q0 + qi) * 128 + 8 * c < w.K;
+        for (int uu = 0; uu < 4; ++uu)
+          c[uu] = ok ? *reinterpret_cast<const uint4 *>(rq + (4 * hb + uu) * kTcUnitBytes + r * 16)
+                     : make_uint4(0u, 0u, 0u, 0u);
+        if (ok) sc = *reinterpret_cast<const uint32_t *>(rq + 8 * kTcUnitBytes + r * 16 + 8 * (Q & 1) + 4 * hb);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[rs]);  // the quad is in registers: its slot may be refilled
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int row = 16 * warp + 2 * i + rp;
-          *reinterpret_cast<uint4 *>(st + row * 128 + (((c & 7) ^ (row & 7)) * 16)) =
-              kin ? dq8(cd[i], __half2half2(__ushort_as_half(sc[i]))) : make_uint4(0u, 0u, 0u, 0u);
+        for (int uu = 0; uu < 4; ++uu) {
+          // columns past K are zero (the scale plane's padding past K / 32 blocks is not)
+          const bool kin = (int64_t)Q * 128 + 16 * (4 * hb + uu) < w.K;
+          const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)((uu >> 1) ? (sc >> 16) : (sc & 0xFFFFu))));
+          const uint4 lo = kin ? dq8(make_uint2(c[uu].x, c[uu].y), d2) : make_uint4(0u, 0u, 0u, 0u);
+          const uint4 hi = kin ? dq8(make_uint2(c[uu].z, c[uu].w), d2) : make_uint4(0u, 0u, 0u, 0u);
+          out[8 * uu + 0] = lo.x;
+          out[8 * uu + 1] = lo.y;
+          out[8 * uu + 2] = lo.z;
+          out[8 * uu + 3] = lo.w;
+          out[8 * uu + 4] = hi.x;
+          out[8 * uu + 5] = hi.y;
+          out[8 * uu + 6] = hi.z;
+          out[8 * uu + 7] = hi.w;
+        }
+      } else {
+        // lane-word t of blocks 2 hb, 2 hb + 1: byte j holds elements 4t + j (low nibble) and 4t + j + 16
+        // (high nibble) of its block
+        uint2 c[4];
+        uint32_t sc = 0u;
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          c[t] = ok ? *reinterpret_cast<const uint2 *>(rq + t * kTcUnitBytes + r * 16 + 8 * hb) : make_uint2(0u, 0u);
+        if (ok) sc = *reinterpret_cast<const uint32_t *>(rq + 4 * kTcUnitBytes + r * 8 + 4 * hb);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[rs]);
+#pragma unroll
+        for (int bi = 0; bi < 2; ++bi) {
+          const __half2 d2 = __half2half2(__ushort_as_half((unsigned short)(bi ? (sc >> 16) : (sc & 0xFFFFu))));
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint32_t wd = bi ? c[t].y : c[t].x;
+            const uint32_t a0 = __byte_perm(wd, 0u, 0x4140), a1 = __byte_perm(wd, 0u, 0x4342);
+            out[16 * bi + 2 * t] = dq_lo(a0, d2);      // elements 4t, 4t+1 of the block
+            out[16 * bi + 2 * t + 1] = dq_lo(a1, d2);  // 4t+2, 4t+3
+            out[16 * bi + 8 + 2 * t] = dq_hi(a0, d2);  // 4t+16, 4t+17
+            out[16 * bi + 9 + 2 * t] = dq_hi(a1, d2);  // 4t+18, 4t+19
+          }
         }
       }
-      fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&afull[as]);
-    }
-  } else if (warp < kTcProducerWarps) {
-    // ================= producers: warp w dequantises strip w, one quad per iteration =================
-    // lane -> (row rr of the strip, lane-word pair tp): a quarter-warp holds 8 consecutive rows of
-    // one pair, so its 16-byte stores into the swizzled rows hit 8 different chunk positions
-    const int tp = (lane >> 3) & 1, rr = (lane & 7) + 8 * (lane >> 4), r = warp * kQ4StripRows + rr;
-    const bool valid = warp < nvalid;
-    for (int qi = 0; qi < nquads; ++qi) {
-      const int rs = qi % R, as = qi % SA;
-      ok = ok && mbar_wait(&rfull[rs], (uint32_t)(qi / R) & 1, scr.err, DEVERR_GEMV_FULL);
-      uint4 U0 = make_uint4(0u, 0u, 0u, 0u), U1 = U0;  // lane-words 2tp, 2tp+1 of blocks 0..3
-      uint2 D = make_uint2(0u, 0u);                     // the four block scales
-      if (ok && valid) {
-        const unsigned char *qb = raw + rs * Geo::RawBytes + warp * kQ4QuadBytes;
-        U0 = *reinterpret_cast<const uint4 *>(qb + (rr * 4 + 2 * tp) * 16);
-        U1 = *reinterpret_cast<const uint4 *>(qb + (rr * 4 + 2 * tp + 1) * 16);
-        D = *reinterpret_cast<const uint2 *>(qb + kQ4QuadCodeBytes + rr * 8);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&rempty[rs]);  // the quad is in registers: its slot may be refilled
       if (qi >= SA) ok = ok && mbar_wait(&aempty[as], (uint32_t)(qi / SA - 1) & 1, scr.err, DEVERR_GEMV_EMPTY);
+      tc_fence_after();
       if (ok) {
-        unsigned char *row = aring + as * kTcAQuad + r * 128;
-        const uint32_t wa[4] = {U0.x, U0.y, U0.z, U0.w}, wb[4] = {U1.x, U1.y, U1.z, U1.w};
-        const uint32_t dd[2] = {D.x, D.y};
-#pragma unroll
-        for (int blk = 0; blk < 4; ++blk) {  // stage blk / 2, columns 32 (blk % 2) .. +31
-          const __half2 d2 = __half2half2(
-              __ushort_as_half((unsigned short)((blk & 1) ? (dd[blk >> 1] >> 16) : (dd[blk >> 1] & 0xFFFFu))));
-          const uint32_t a0 = __byte_perm(wa[blk], 0u, 0x4140), a1 = __byte_perm(wa[blk], 0u, 0x4342);
-          const uint32_t b0 = __byte_perm(wb[blk], 0u, 0x4140), b1 = __byte_perm(wb[blk], 0u, 0x4342);
-          // low nibbles: elements 8tp..8tp+7 -> chunk 4 (blk % 2) + tp; high: 16 + 8tp.. -> chunk + 2
-          const int clo = (blk & 1) * 4 + tp, chi = clo + 2;
-          unsigned char *st = row + (blk >> 1) * (kTcRows * 128);
-          *reinterpret_cast<uint4 *>(st + ((clo ^ (r & 7)) * 16)) =
-              make_uint4(dq_lo(a0, d2), dq_lo(a1, d2), dq_lo(b0, d2), dq_lo(b1, d2));
-          *reinterpret_cast<uint4 *>(st + ((chi ^ (r & 7)) * 16)) =
-              make_uint4(dq_hi(a0, d2), dq_hi(a1, d2), dq_hi(b0, d2), dq_hi(b1, d2));
-        }
+        const uint32_t ts = ta + as * kTcACols;
+        tmem_st16_issue(ts, *reinterpret_cast<const uint32_t(*)[16]>(&out[0]));
+        tmem_st16_issue(ts + 16, *reinterpret_cast<const uint32_t(*)[16]>(&out[16]));
+        tmem_st_wait();
       }
-      fence_proxy_async_smem();  // the tensor core reads these bytes through the async proxy
+      tc_fence_before();  // the MMA reads these TMEM columns after the barrier below
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[as]);
     }
   } else if (warp == kTcMmaWarp) {
-    // ================= MMA issuer: 8 MMAs (K = 16 each) per quad =================
+    // ================= MMA issuer: 8 MMAs (K = 16 each, A from TMEM) per quad =================
     if (lane == 0) {
       const uint32_t idesc = idesc_f16<NT>();
       for (int qi = 0; qi < nquads; ++qi) {
@@ -278,36 +275,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         ok = ok && mbar_wait(&afull[as], (uint32_t)(qi / SA) & 1, scr.err, DEVERR_GEMV_FULL);
         tc_fence_after();
         if (ok) {
-          const uint32_t a = smem_u32(aring + as * kTcAQuad), bq = smem_u32(bring + bs * Geo::BQuad);
+          const uint32_t bq = smem_u32(bring + bs * Geo::BQuad), ta = taddr + Geo::ACol + as * kTcACols;
 #pragma unroll
           for (int h = 0; h < 2; ++h)
 #pragma unroll
-            for (int kk = 0; kk < kTcK / 16; ++kk)  // 32 bytes further into the swizzle atom per K = 16
-              umma_f16(taddr, smem_desc_sw128(a + h * (kTcRows * 128) + 32 * kk),
-                       smem_desc_sw128(bq + h * (NT * 128) + 32 * kk), idesc, (qi > 0 || h > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < kTcK / 16; ++kk)  // K = 64 h + 16 kk: 8 A columns, 32 bytes into the B atom
+              umma_f16_tmem_a(taddr, ta + 8 * (4 * h + kk), smem_desc_sw128(bq + h * (NT * 128) + 32 * kk), idesc,
+                              (qi > 0 || h > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(&aempty[as]);  // frees the A and B slots once the MMAs above have read them
+        umma_commit(&aempty[as]);  // frees the A and B stages once the MMAs above have read them
         umma_commit(&bempty[bs]);
       }
       umma_commit(&accum);
     }
   } else if (warp == kTcRawWarp) {
-    // ================= raw loader: one 3-D box per quad (8 strips), up to R ahead =================
+    // ================= raw loader: one quad of 128 rows per slot, up to R ahead =================
     if (lane == 0) {
       const uint64_t pol_w = l2_evict_first_policy();
       tma_prefetch_desc(&tmw);
+      tma_prefetch_desc(&tms);
+      const int strip0 = tile_n * (kTcRows / kQ4StripRows);
       int issued = 0;
       for (int qi = 0; qi < nquads; ++qi) {
-        const int rs = qi % R;
+        const int rs = qi % R, Q = q0 + qi;
         if (qi >= R) ok = ok && mbar_wait(&rempty[rs], (uint32_t)(qi / R - 1) & 1, scr.err, DEVERR_GEMV_EMPTY);
-        if (ok) {  // strips (rows) past N and codes past K read as zero
+        if (ok) {  // rows past N and codes past K read as zero
+          unsigned char *dst = raw + rs * Geo::RawBytes;
           mbar_arrive_expect_tx(&rfull[rs], (uint32_t)Geo::RawBytes);
-          if (Geo::Q8) {
-            tma_load_2d(raw + rs * Geo::RawBytes, &tmw, 128 * (q0 + qi), tile_n * kTcRows, &rfull[rs], pol_w);
-            tma_load_2d(raw + rs * Geo::RawBytes + kTcQ8CodeBytes, &tms, 8 * ((q0 + qi) >> 1), tile_n * kTcRows,
-                        &rfull[rs], pol_w);
+          if constexpr (Geo::Q8) {
+            for (int u = 0; u < 8; ++u)
+              tma_load_2d(dst + u * kTcUnitBytes, &tmw, 128 * Q + 16 * u, tile_n * kTcRows, &rfull[rs], pol_w);
+            tma_load_2d(dst + 8 * kTcUnitBytes, &tms, 8 * (Q >> 1), tile_n * kTcRows, &rfull[rs], pol_w);
           } else {
-            tma_load_3d(raw + rs * Geo::RawBytes, &tmw, 0, q0 + qi, (int32_t)strip0, &rfull[rs], pol_w);
+            for (int t = 0; t < 4; ++t)
+              tma_load_4d(dst + t * kTcUnitBytes, &tmw, 4 * t, 0, Q, strip0, &rfull[rs], pol_w);
+            tma_load_3d(dst + 4 * kTcUnitBytes, &tms, 0, Q, strip0, &rfull[rs], pol_w);
           }
           issued = qi + 1;
         } else {
@@ -419,16 +421,16 @@ void launch_tc_t(const QMat &w, const float *x, int M, int64_t ldx, const Epilog
   const int nq = Geo::Q8 ? (int)ceil_div(w.K, 128) : (int)w.row_words;  // K split in whole quads, >= 4 per split
   int splits = 1;
   const int tiles = tiles_n * tiles_m;
+  const int slots = num_sms * (Geo::Two ? 2 : 1);  // resident CTAs
   // split K to minimise waves x (quads per CTA + a fixed per-CTA cost of about 4 quads: TMEM
-  // allocation, pipeline fill, epilogue, fix-up); e.g. 86 tiles of 32 quads on 148 SMs run 3 splits
-  // in 2 waves (2 x 15) rather than 1 split in 1 wave (36)
-  if (tiles < 2 * num_sms) {
-    int best = (tiles + num_sms - 1) / num_sms * (nq + 4);
-    for (int s = 2; s <= std::min(16, nq / 4); ++s) {
-      const int cost = (tiles * s + num_sms - 1) / num_sms * ((nq + s - 1) / s + 4);
+  // allocation, pipeline fill, epilogue, fix-up)
+  if (tiles < 2 * slots) {
+    int best = (tiles + slots - 1) / slots * (nq + 4);
+    for (int sp = 2; sp <= std::min(16, nq / 4); ++sp) {
+      const int cost = (tiles * sp + slots - 1) / slots * ((nq + sp - 1) / sp + 4);
       if (cost < best) {
         best = cost;
-        splits = s;
+        splits = sp;
       }
     }
   }
@@ -457,20 +459,28 @@ void launch_tc_t(const QMat &w, const float *x, int M, int64_t ldx, const Epilog
   const CUtensorMap tmx = make_tmap_3d(sc.xh, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kTcK, (uint64_t)M,
                                        (uint64_t)(Kp / kTcK), (uint64_t)Kp * 2, kTcK * 2, kTcK, NT, 2,
                                        CU_TENSOR_MAP_SWIZZLE_128B);
-  // A operand source.  Q4_0: the strips as [strip][quad][1152 bytes], one quad of 8 strips per box.
-  // Q8_0: the codes [N][K] (boxes of 128 rows x 128 codes) and the scales [N][ldd] fp16 (boxes of
-  // 128 rows x 8 scales, two quads)
+  // A operand sources, each box landing as [rows][16 bytes]:
+  //  Q4_0: the strips [strip][quad][16 rows][4 lane-words][4 blocks] u32 -> for lane-word t one box
+  //        (4 words at t, 16 rows, 1 quad, 8 strips); the scales at byte 1024 of each strip-quad,
+  //        [16 rows][4] fp16 -> one box (128 bytes, 1 quad, 8 strips)
+  //  Q8_0: the codes [N][K] (boxes of 128 rows x 16 codes) and the scales [N][ldd] fp16 (boxes of
+  //        128 rows x 8 scales, two quads)
   CUtensorMap tmw, tms;
   if (Geo::Q8) {
     tmw = make_tmap_2d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, (uint64_t)w.N, (uint64_t)w.row_words * 4,
-                       (uint64_t)w.row_words * 4, kTcRows, 128);
+                       (uint64_t)w.row_words * 4, kTcRows, 16);
     tms = make_tmap_2d(w.d, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, (uint64_t)w.N, (uint64_t)w.ldd, (uint64_t)w.ldd * 2,
                        kTcRows, 8);
   } else {
-    tmw = make_tmap_3d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT64, 8, kQ4QuadBytes / 8, (uint64_t)nq,
-                       (uint64_t)q4_strips(w.N), kQ4QuadBytes, (uint64_t)nq * kQ4QuadBytes, kQ4QuadBytes / 8, 1,
+    const uint64_t strips = (uint64_t)q4_strips(w.N);
+    const uint64_t dims[4] = {16, kQ4StripRows, (uint64_t)nq, strips};
+    const uint64_t strides[3] = {64, kQ4QuadBytes, (uint64_t)nq * kQ4QuadBytes};
+    const uint32_t box[4] = {4, kQ4StripRows, 1, kTcRows / kQ4StripRows};
+    tmw = make_tmap_4d(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, dims, strides, box);
+    tms = make_tmap_3d(reinterpret_cast<const unsigned char *>(w.qs) + kQ4QuadCodeBytes, CU_TENSOR_MAP_DATA_TYPE_UINT32,
+                       4, (kQ4QuadBytes - kQ4QuadCodeBytes) / 4, (uint64_t)nq, strips, kQ4QuadBytes,
+                       (uint64_t)nq * kQ4QuadBytes, (kQ4QuadBytes - kQ4QuadCodeBytes) / 4, 1,
                        kTcRows / kQ4StripRows);
-    tms = tmw;
   }
   const size_t smem = Geo::Smem;
   static unsigned long long attr_set = 0;

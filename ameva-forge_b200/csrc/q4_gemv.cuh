@@ -184,64 +184,80 @@ __device__ __forceinline__ void q4_stage_x(const Q4X<MV> &X, const float *x, int
                                            int nth, float *ss_out) {
   const int lane = tid & 31, warp = tid >> 5;
   const int q = lane & 7;  // 4-element group of the block
+  constexpr int U = 4;     // items whose x (and gamma) loads are in flight together
 #pragma unroll
   for (int m = 0; m < MV; ++m) {
     float ss = 0.0f;
-    for (int item = tid; item < X.nbx * 8; item += nth) {
-      const int bb = item >> 3;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (bb < X.nb) {
-        const int k = bb * 32 + 4 * q;
-        v = __ldcg(reinterpret_cast<const float4 *>(x + m * ldx + k));
-        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    // nbx * 8 items is a multiple of 32 and nth a multiple of 32: an item index is valid for a whole warp or
+    // for none of its lanes, so the shuffles below always run warp-wide
+    for (int base = tid; base < X.nbx * 8; base += U * nth) {
+      float4 v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int item = base + u * nth, bb = item >> 3;
+        v[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (item < X.nbx * 8 && bb < X.nb) v[u] = __ldcg(reinterpret_cast<const float4 *>(x + m * ldx + bb * 32 + 4 * q));
+      }
+      float4 g[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int item = base + u * nth, bb = item >> 3;
+        g[u] = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (gamma && item < X.nbx * 8 && bb < X.nb) g[u] = *reinterpret_cast<const float4 *>(gamma + bb * 32 + 4 * q);
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int item = base + u * nth, bb = item >> 3;
+        if (item >= X.nbx * 8) break;  // warp-uniform
+        float4 vv = v[u];
+        ss += vv.x * vv.x + vv.y * vv.y + vv.z * vv.z + vv.w * vv.w;
         if (gamma) {
-          const float4 g = *reinterpret_cast<const float4 *>(gamma + k);
-          v.x *= g.x;
-          v.y *= g.y;
-          v.z *= g.z;
-          v.w *= g.w;
+          vv.x *= g[u].x;
+          vv.y *= g[u].y;
+          vv.z *= g[u].z;
+          vv.w *= g[u].w;
         }
-      }
-      float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
-      // amax in [2^E, 2^(E+1)) -> scale 2^(20 - E); zero / subnormal blocks keep 2^126 (digits ~0)
-      const int E = ((__float_as_int(amax) >> 23) & 0xFF) - 127;
-      const int e = min(max(20 - E, -126), 126);
-      const float scl = __int_as_float((e + 127) << 23);
-      const float vf[4] = {v.x, v.y, v.z, v.w};
-      int hi[4], mi[4], lo[4], shi = 0, smi = 0, slo = 0;
+        float amax = fmaxf(fmaxf(fabsf(vv.x), fabsf(vv.y)), fmaxf(fabsf(vv.z), fabsf(vv.w)));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+        // amax in [2^E, 2^(E+1)) -> scale 2^(20 - E); zero / subnormal blocks keep 2^126 (digits ~0)
+        const int E = ((__float_as_int(amax) >> 23) & 0xFF) - 127;
+        const int e = min(max(20 - E, -126), 126);
+        const float scl = __int_as_float((e + 127) << 23);
+        const float vf[4] = {vv.x, vv.y, vv.z, vv.w};
+        int hi[4], mi[4], lo[4], shi = 0, smi = 0, slo = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int vi = __float2int_rn(fminf(fmaxf(vf[i] * scl, -2097152.0f), 2097151.0f));
-        hi[i] = vi >> 14;
-        mi[i] = (vi >> 7) & 127;
-        lo[i] = vi & 127;
-        shi += hi[i];
-        smi += mi[i];
-        slo += lo[i];
-      }
-      // B fragment words of digit columns 3m, 3m+1, 3m+2: lane-word t = q & 3, half q >> 2
-      uint32_t *col = reinterpret_cast<uint32_t *>(X.xb + (bb * 3 * MV + 3 * m) * 4) + (q & 3) * 2 + (q >> 2);
-      col[0] = pack_s8x4(hi[0], hi[1], hi[2], hi[3]);
-      col[8] = pack_s8x4(mi[0], mi[1], mi[2], mi[3]);
-      col[16] = pack_s8x4(lo[0], lo[1], lo[2], lo[3]);
+        for (int i = 0; i < 4; ++i) {
+          const int vi = __float2int_rn(fminf(fmaxf(vf[i] * scl, -2097152.0f), 2097151.0f));
+          hi[i] = vi >> 14;
+          mi[i] = (vi >> 7) & 127;
+          lo[i] = vi & 127;
+          shi += hi[i];
+          smi += mi[i];
+          slo += lo[i];
+        }
+        // B fragment words of digit columns 3m, 3m+1, 3m+2: lane-word t = q & 3, half q >> 2
+        uint32_t *col = reinterpret_cast<uint32_t *>(X.xb + (bb * 3 * MV + 3 * m) * 4) + (q & 3) * 2 + (q >> 2);
+        col[0] = pack_s8x4(hi[0], hi[1], hi[2], hi[3]);
+        col[8] = pack_s8x4(mi[0], mi[1], mi[2], mi[3]);
+        col[16] = pack_s8x4(lo[0], lo[1], lo[2], lo[3]);
 #pragma unroll
-      for (int o = 1; o < 8; o <<= 1) {
-        shi += __shfl_xor_sync(0xffffffffu, shi, o);
-        smi += __shfl_xor_sync(0xffffffffu, smi, o);
-        slo += __shfl_xor_sync(0xffffffffu, slo, o);
-      }
-      if (q == 0) {
-        // C of the lanes holding (hi, mid) and (lo, 0) of token m
-        X.cx0[(2 * m) * X.nbx + bb] = -8 * shi;
-        X.cx1[(2 * m) * X.nbx + bb] = -8 * smi;
-        X.cx0[(2 * m + 1) * X.nbx + bb] = -8 * slo;
-        X.cx1[(2 * m + 1) * X.nbx + bb] = 0;
-        // non-finite inputs make the block factor NaN, so the outputs are NaN
-        X.fbk[m * X.nbx + bb] =
-            amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000);
+        for (int o = 1; o < 8; o <<= 1) {
+          shi += __shfl_xor_sync(0xffffffffu, shi, o);
+          smi += __shfl_xor_sync(0xffffffffu, smi, o);
+          slo += __shfl_xor_sync(0xffffffffu, slo, o);
+        }
+        if (q == 0) {
+          // C of the lanes holding (hi, mid) and (lo, 0) of token m
+          X.cx0[(2 * m) * X.nbx + bb] = -8 * shi;
+          X.cx1[(2 * m) * X.nbx + bb] = -8 * smi;
+          X.cx0[(2 * m + 1) * X.nbx + bb] = -8 * slo;
+          X.cx1[(2 * m + 1) * X.nbx + bb] = 0;
+          // non-finite inputs make the block factor NaN, so the outputs are NaN
+          X.fbk[m * X.nbx + bb] =
+              amax <= 3.402823466e38f ? __int_as_float((127 - e) << 23) : __int_as_float(0x7fc00000);
+        }
       }
     }
     ss = warp_sum(ss);
