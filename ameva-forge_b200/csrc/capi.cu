@@ -769,7 +769,7 @@ int fg_flash_attention(fg_ctx *ctx, fg_handle q, fg_handle k, fg_handle v, float
   a.scale = has_scale ? scale : (float)(1.0 / std::sqrt((double)d));
   a.causal = causal ? 1 : 0;
   a.err = c.gemv.err;
-  launch_attention(a, c.num_sms, c.stream);
+  launch_attention(c, a, c.stream);
   *out = h;
   FG_API_END
 }

@@ -846,7 +846,7 @@ fg_handle Exec::exec_node(size_t i, const void *const *inputs, const uint64_t *i
     a.scale = scale;
     a.causal = causal;
     a.err = c.gemv.err;
-    if (n.numel) launch_attention(a, c.num_sms, s);
+    if (n.numel) launch_attention(c, a, s);
     return h;
   }
   if (op == "axpy" || op == "adam_step" || op == "sgd_momentum_step")

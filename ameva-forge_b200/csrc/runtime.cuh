@@ -216,6 +216,10 @@ struct AttnArgs {
   int *err = nullptr;                    // device error word of bounded waits (tensor-core path)
 };
 void launch_attention(const AttnArgs &a, int num_sms, cudaStream_t s);
+// attention_tc32.cu: fp32 K/V on the tensor cores (fp16 hi/lo splits of Q and K, range-scaled per head
+// and query row, in scratch from the context pool) where the shape allows, else launch_attention above.
+bool attn_tc32_supported(const AttnArgs &a);
+void launch_attention(Ctx &c, const AttnArgs &a, cudaStream_t s);
 // attention_tc.cu: tcgen05 flash attention (fp16 K/V, head_dim 64 or 128,
 // 16-byte aligned rows).  K/V past the live length up to the cache extent
 // (kv_sh / d tokens) are read in whole 128-key blocks and masked, so they must

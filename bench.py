@@ -62,7 +62,7 @@ def parse():
                     help="profiling case M,N,K: `warmup` + `steps` launches of one Q4_0 GEMM (x [M,K] fp32, "
                          "W [N,K]); prints its event-timed launch time")
     ap.add_argument("--attention-case", default="",
-                    help="flash-attention prefill B,H,S,d (causal, fp16 Q/K/V ~ N(0,1), scale 1/sqrt(d)): "
+                    help="flash-attention prefill B,H,S,d[,f32] (causal, fp16 (or fp32) Q/K/V ~ N(0,1), scale 1/sqrt(d)): "
                          "`warmup` + `steps` calls; prints TFLOP/s and the tensor-core fraction")
     ap.add_argument("--decode-table", action="store_true",
                     help="decode rows of the scope table: TinyLlama-1.1B shape b1 ctx 2048 (256 tokens), "
@@ -396,9 +396,11 @@ def gemm_case(ctx, spec, warmup, steps):
 def attention_case(ctx, spec, warmup, steps):
     """Causal flash-attention prefill on seeded fp16 inputs [B, H, S, d], timed
     with CUDA events on the library stream (FLOPs = 4 B H S^2 d / 2)."""
-    B, H, S, d = (int(v) for v in spec.split(","))
+    parts = spec.split(",")
+    B, H, S, d = (int(v) for v in parts[:4])
+    dt = np.float32 if len(parts) > 4 and parts[4] == "f32" else np.float16  # f32: the executeGraph path
     stream = torch.cuda.ExternalStream(ctx.stream_ptr())
-    q, k, v = (ctx.synth_normal((B, H, S, d), np.float16, seed=SEED + i) for i in range(3))
+    q, k, v = (ctx.synth_normal((B, H, S, d), dt, seed=SEED + i) for i in range(3))
     for _ in range(warmup):
         ctx.dispose(ctx.flashAttention(q, k, v, isCausal=True))
     # each output goes back to the stream-ordered pool right after its call, so every call reuses one
@@ -416,7 +418,8 @@ def attention_case(ctx, spec, warmup, steps):
     flops = 4.0 * B * H * S * S * d / 2
     with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
         peak_tf = float(json.load(f).get("bf16_tflops", 1590.0))
-    return {"attention_case": {"B": B, "H": H, "S": S, "d": d, "causal": True, "dtype": "fp16 in, fp32 out"},
+    return {"attention_case": {"B": B, "H": H, "S": S, "d": d, "causal": True,
+                               "dtype": ("fp32" if dt == np.float32 else "fp16") + " in, fp32 out"},
             "calls": warmup + steps, "ms_per_call": ms, "TFLOPs": flops / ms / 1e9,
             "tensor_frac": flops / ms / 1e9 / peak_tf, "peak_TFLOPs": peak_tf,
             "path": os.environ.get("FORGE_B200_ATTN", "tcgen05")}
