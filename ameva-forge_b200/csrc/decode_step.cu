@@ -363,9 +363,9 @@ struct AttnCfg {
   static constexpr int GL = 8 / G;               // lanes of a key that end the score reduction with the same g
   static constexpr bool QREG = G * NV * 8 <= 32;  // this lane's q slice lives in registers
   // shared scratch (floats): q [G][D] (chunk halves swizzled), per-warp p [8][G][4] + alpha [8][G],
-  // warp states (m, l) [8][G] and o [8][G][D]; the cross-split merge reuses the o area for its weights
+  // warp states (m, l) [8][G], o [8][G][D] and the K and V rows of this step's key (D fp16 each)
   static constexpr int SM_Q = 0, SM_P = G * D, SM_ML = r4(SM_P + 8 * G * 5), SM_O = r4(SM_ML + 16 * G),
-                       SM_END = SM_O + 8 * G * D;
+                       SM_KV = SM_O + 8 * G * D, SM_END = SM_KV + D;
 };
 
 // Offset of q element dd of a row: the two float4 halves of 8-dim chunk k swap places when bit 2 of k is
@@ -565,10 +565,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   unsigned char *base = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
   __shared__ __align__(8) uint64_t full[kStepGroups][kStepStages], empty[kStepGroups][kStepStages];
   __shared__ float s_sum[(kStepConsumers / 32)];
-  __shared__ float s_inv;
   __shared__ int s_last[kStepGroups];
   __shared__ int s_abort;
   __shared__ unsigned long long s_key[kStepConsumers / 32];
+  __shared__ float s_rope[128];  // cos / sin of every RoPE frequency at this step's position (head_dim <= 128)
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int per = 5;  // QKV, ATTN, O, GATEUP, DOWN (tensor parallelism folds its exchanges into staging)
@@ -623,6 +623,13 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   }
 
   // =========================== consumers ===========================
+  // the QKV epilogues' RoPE factors, once per launch (the first QKV phase follows at least one barrier)
+  for (int f = tid; f < A.d / 2; f += kStepConsumers) {
+    float sn, cs;
+    sincosf(rope_theta(A.inv_freq[f], npos), &sn, &cs);
+    s_rope[f] = cs;
+    s_rope[A.d / 2 + f] = sn;
+  }
   const int grp = warp / kGroupWarps, gw = warp % kGroupWarps, gtid = tid % kGroupThreads;
   const int vk = blockIdx.x * kStepGroups + grp;
   const int gbar = 1 + grp;
@@ -650,6 +657,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
         const bool last = s == sp.S - 1;
         for (int e = gtid; e < G * D; e += kGroupThreads)
           sm[Cf::SM_Q + (e / D) * D + q_swz(e % D)] = __ldcg(A.q + (int64_t)hk * G * D + e) * A.scale;
+        if (last && gtid < D / 4) {  // key npos (written by this launch's QKV phase): K then V row, 16 B each
+          const int64_t row = ((int64_t)hk * A.cap + npos) * D;
+          const __half *src = (gtid < D / 8 ? A.layers[l].k : A.layers[l].v) + row + (gtid % (D / 8)) * 8;
+          reinterpret_cast<uint4 *>(sm + Cf::SM_KV)[gtid] = __ldcg(reinterpret_cast<const uint4 *>(src));
+        }
         named_sync_id(gbar, kGroupThreads);
         WarpAttn<D, G> W;
         attn_warp_init<D, G>(W, sm + Cf::SM_Q, lane);
@@ -665,9 +677,9 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
           __syncwarp();
           if (lane == 0) mbar_arrive(&em[sl]);
         }
-        if (last && gw == 0 && ok) {  // key npos: this step's K/V, written by the QKV phase of this launch
-          const int64_t row = ((int64_t)hk * A.cap + npos) * D;
-          attn_warp_tile<D, G, true>(A.layers[l].k + row, A.layers[l].v + row, 1, sm + Cf::SM_Q, wp, W, 0, lane);
+        if (last && gw == 0 && ok) {  // key npos: this step's K/V, staged with q
+          const __half *kv = reinterpret_cast<const __half *>(sm + Cf::SM_KV);
+          attn_warp_tile<D, G, false>(kv, kv + D, 1, sm + Cf::SM_Q, wp, W, 0, lane);
         }
         // ---- merge the eight warp states into the unit's (m, l, o)
         float *wml = sm + Cf::SM_ML, *wo = sm + Cf::SM_O;
@@ -798,6 +810,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
       const float *x, *gm;
       Epilogue ep;
       gemv_phase(A, ph, l, w, x, gm, ep);
+      if (ph == PH_QKV) {
+        ep.rope_cs = s_rope;
+        ep.pos0 = npos;
+      }
       const Sched sc = make_sched(w.N, kQ4StripRows, 1, vk, P);  // units = 16-row strips
       const int nq = (int)w.row_words;
       Q4X<1> X;
@@ -821,8 +837,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
         q4_stage_x<1>(X, x, w.K, gm, tid, kStepConsumers, s_sum);
       }
       named_sync_id(kBarConsumers, kStepConsumers);
-      if (tid == 0) s_inv = rms_inv(s_sum, kStepConsumers / 32, 1, 0, w.K, A.eps, gm != nullptr);
-      named_sync_id(kBarConsumers, kStepConsumers);
+      // every thread forms 1/rms from the warps' sums (s_sum is rewritten only after the phase's barrier)
+      const float inv = rms_inv(s_sum, kStepConsumers / 32, 1, 0, w.K, A.eps, gm != nullptr);
       Q4Lane<1> Ln;
       Ln.init(X, lane);
       float2 acc[1] = {make_float2(0.0f, 0.0f)};
@@ -839,7 +855,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
         float *rb = red + ((u - sc.u0) & 1) * (kGroupWarps * kQ4StripRows);
         q4_group_red<1>(rb, acc, gw, lane);
         named_sync_id(gbar, kGroupThreads);
-        if (ok) finish_strip<1, TP>(w, ep, u, rb, &s_inv, gtid, kGroupThreads);
+        if (ok) finish_strip<1, TP>(w, ep, u, rb, &inv, gtid, kGroupThreads);
       }
     }
     // ---------------- end of phase: grid barrier

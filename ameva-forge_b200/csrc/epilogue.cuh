@@ -7,12 +7,22 @@
 namespace fg {
 
 // Interleaved-pair RoPE of one (v0, v1) pair: rope.wgsl.ts:45-59 (theta in fp32).
-__device__ inline void rope_pair(float v0, float v1, float inv_freq, int pos, float &o0, float &o1) {
-  float theta = __fmul_rn(inv_freq, (float)pos);
-  float s, c;
-  sincosf(theta, &s, &c);
+__device__ inline float rope_theta(float inv_freq, int pos) { return __fmul_rn(inv_freq, (float)pos); }
+__device__ inline void rope_rot(float v0, float v1, float c, float s, float &o0, float &o1) {
   o0 = __fsub_rn(__fmul_rn(v0, c), __fmul_rn(v1, s));
   o1 = __fadd_rn(__fmul_rn(v1, c), __fmul_rn(v0, s));
+}
+__device__ inline void rope_pair(float v0, float v1, float inv_freq, int pos, float &o0, float &o1) {
+  float s, c;
+  sincosf(rope_theta(inv_freq, pos), &s, &c);
+  rope_rot(v0, v1, c, s, o0, o1);
+}
+// RoPE of frequency i: from the epilogue's table when it has one (same theta, same sincosf).
+__device__ inline void rope_pair_ep(const Epilogue &ep, float v0, float v1, int i, int pos, float &o0, float &o1) {
+  if (ep.rope_cs)
+    rope_rot(v0, v1, ep.rope_cs[i], ep.rope_cs[(ep.head_dim >> 1) + i], o0, o1);
+  else
+    rope_pair(v0, v1, ep.inv_freq[i], pos, o0, o1);
 }
 
 // SwiGLU: swiglu.wgsl.ts:38-40, gate / (1 + exp(-gate)) * up.
@@ -48,10 +58,10 @@ __device__ inline void epi_store_pair(const Epilogue &ep, int64_t n, int m, floa
   } else {  // EPI_QKV
     const int d = ep.head_dim;
     const int b = m / ep.tokens_per_seq;
-    const int pos = ep.pos[b] + (m - b * ep.tokens_per_seq);
+    const int pos = ep.rope_cs ? ep.pos0 : ep.pos[b] + (m - b * ep.tokens_per_seq);
     if (n < ep.n_q) {
       float o0, o1;
-      rope_pair(v0, v1, ep.inv_freq[(n % d) >> 1], pos, o0, o1);
+      rope_pair_ep(ep, v0, v1, (int)((n % d) >> 1), pos, o0, o1);
       float *q = ep.q_out + (int64_t)m * ep.n_q + n;
       q[0] = o0;
       q[1] = o1;
@@ -66,7 +76,7 @@ __device__ inline void epi_store_pair(const Epilogue &ep, int64_t n, int m, floa
         *reinterpret_cast<__half2 *>(ep.v_cache + idx) = __halves2half2(__float2half_rn(v0), __float2half_rn(v1));
       } else {
         float o0, o1;
-        rope_pair(v0, v1, ep.inv_freq[c >> 1], pos, o0, o1);
+        rope_pair_ep(ep, v0, v1, (int)(c >> 1), pos, o0, o1);
         *reinterpret_cast<__half2 *>(ep.k_cache + idx) = __halves2half2(__float2half_rn(o0), __float2half_rn(o1));
       }
     }

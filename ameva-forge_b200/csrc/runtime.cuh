@@ -164,6 +164,10 @@ struct Epilogue {
   int tokens_per_seq = 1;        // token m belongs to sequence m / tokens_per_seq
   const int *pos = nullptr;      // [B] cache length before this forward
   const float *inv_freq = nullptr;  // [head_dim/2]
+  // single-token QKV (the persistent decode step): cos / sin of every frequency at position pos0,
+  // cos at [i], sin at [head_dim/2 + i], computed once per launch (null: sincosf per pair)
+  const float *rope_cs = nullptr;
+  int pos0 = 0;
   // XCHG (tensor-parallel partial sums): column n goes to xdst[r] + xoff + n for every rank r < nx
   float *const *xdst = nullptr;
   int64_t xoff = 0;
