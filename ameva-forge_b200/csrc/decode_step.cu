@@ -197,9 +197,9 @@ __device__ __noinline__ bool exchange_keys(const StepArgs &A, unsigned long long
   return true;
 }
 
-// GEMV operand of phase p (layer l).
-__device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, QMat &w, const float *&x,
-                                           const float *&gamma, Epilogue &ep) {
+// GEMV operand of phase p (layer l, whose weights and cache `lay` describes; unused for LM_HEAD).
+__device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, const StepLayer *lay, QMat &w,
+                                           const float *&x, const float *&gamma, Epilogue &ep) {
   const auto xchg = [&](Epilogue &e, int xi) {  // partial sums to every rank's part[xi % 2][this rank]
     e.mode = EPI_XCHG;
     e.xdst = A.xr;
@@ -216,7 +216,7 @@ __device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, Q
     ep.ldy = A.vocab_l;
     return;
   }
-  const StepLayer &Ly = A.layers[l];
+  const StepLayer &Ly = *lay;
   switch (ph) {
     case PH_QKV:
       w = Ly.qkv;
@@ -331,7 +331,7 @@ struct StepCursor {
         QMat w;
         const float *x, *gm;
         Epilogue ep;
-        gemv_phase(*A, ph, l, w, x, gm, ep);
+        gemv_phase(*A, ph, l, A->layers + l, w, x, gm, ep);
         const Sched sc = make_sched(w.N, kQ4StripRows, 1, vk, P);
         src = reinterpret_cast<const unsigned char *>(w.qs);
         nq = (int)w.row_words;
@@ -569,6 +569,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   __shared__ int s_abort;
   __shared__ unsigned long long s_key[kStepConsumers / 32];
   __shared__ float s_rope[128];  // cos / sin of every RoPE frequency at this step's position (head_dim <= 128)
+  // descriptors of layer l in slot l & 1: copied ahead of the barrier before the layer's first phase, so the
+  // phase starts without a global-memory round trip
+  __shared__ __align__(16) StepLayer s_layer[2];
+  static_assert(sizeof(StepLayer) % 16 == 0 && sizeof(StepLayer) / 16 <= kStepConsumers, "layer copy");
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   constexpr int per = 5;  // QKV, ATTN, O, GATEUP, DOWN (tensor parallelism folds its exchanges into staging)
@@ -630,6 +634,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
     s_rope[f] = cs;
     s_rope[A.d / 2 + f] = sn;
   }
+  if (tid < (int)(sizeof(StepLayer) / 16))
+    reinterpret_cast<uint4 *>(&s_layer[0])[tid] = reinterpret_cast<const uint4 *>(A.layers)[tid];
   const int grp = warp / kGroupWarps, gw = warp % kGroupWarps, gtid = tid % kGroupThreads;
   const int vk = blockIdx.x * kStepGroups + grp;
   const int gbar = 1 + grp;
@@ -659,7 +665,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
           sm[Cf::SM_Q + (e / D) * D + q_swz(e % D)] = __ldcg(A.q + (int64_t)hk * G * D + e) * A.scale;
         if (last && gtid < D / 4) {  // key npos (written by this launch's QKV phase): K then V row, 16 B each
           const int64_t row = ((int64_t)hk * A.cap + npos) * D;
-          const __half *src = (gtid < D / 8 ? A.layers[l].k : A.layers[l].v) + row + (gtid % (D / 8)) * 8;
+          const __half *src = (gtid < D / 8 ? s_layer[l & 1].k : s_layer[l & 1].v) + row + (gtid % (D / 8)) * 8;
           reinterpret_cast<uint4 *>(sm + Cf::SM_KV)[gtid] = __ldcg(reinterpret_cast<const uint4 *>(src));
         }
         named_sync_id(gbar, kGroupThreads);
@@ -809,7 +815,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
       QMat w;
       const float *x, *gm;
       Epilogue ep;
-      gemv_phase(A, ph, l, w, x, gm, ep);
+      gemv_phase(A, ph, l, &s_layer[l & 1], w, x, gm, ep);
       if (ph == PH_QKV) {
         ep.rope_cs = s_rope;
         ep.pos0 = npos;
@@ -860,6 +866,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
     }
     // ---------------- end of phase: grid barrier
     if (!ok) s_abort = 1;
+    if (ph == PH_DOWN && l + 1 < L && tid < (int)(sizeof(StepLayer) / 16))  // the next layer's descriptors
+      reinterpret_cast<uint4 *>(&s_layer[(l + 1) & 1])[tid] = reinterpret_cast<const uint4 *>(A.layers + l + 1)[tid];
     named_sync_id(kBarConsumers, kStepConsumers);
     const bool xphase = TP && (ph == PH_O || ph == PH_DOWN);
     const unsigned long long btarget = (epoch * (unsigned long long)nphase + p + 1) * gridDim.x;
