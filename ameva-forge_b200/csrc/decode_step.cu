@@ -33,7 +33,10 @@
 //
 // Every wait is bounded (2 s): a barrier that times out sets the device error
 // word, and all threads then leave without further waiting.
+#include <type_traits>
+
 #include "q4_gemv.cuh"
+#include "tmap.cuh"
 
 namespace fg {
 
@@ -44,6 +47,11 @@ constexpr int kStepGroups = 2;                                   // virtual CTAs
 constexpr int kStepConsumers = kStepGroups * kGroupThreads;      // 512
 constexpr int kStepThreads = kStepConsumers + kStepGroups * 32;  // + one producer warp per group
 constexpr int kKeysPerTile = 32;
+constexpr int kBoxBytes = kKeysPerTile * 128;  // one [32 keys][64 dims] fp16 box of an attention tile
+// GQA groups of 4 and 8 fill half or all of the 8 columns of the attention tile on tensor cores: they take it
+// (groups of 1 and 2 take the CUDA-core tile).
+template <int G>
+constexpr bool kMmaAttn = G >= 4;
 constexpr int kBarConsumers = 3;                                 // named barrier of all consumer warps
 
 enum Phase { PH_EMBED, PH_QKV, PH_ATTN, PH_O, PH_GATEUP, PH_DOWN, PH_LM, PH_ARGMAX };
@@ -268,17 +276,17 @@ __device__ __forceinline__ void gemv_phase(const StepArgs &A, Phase ph, int l, c
 namespace {
 
 // The ring stages one virtual CTA's producer fills over a whole launch, in consumption order: GEMV phases
-// give the tiles of its strips (one contiguous copy each), ATTN phases the K and V rows of its unit's
-// 32-key tiles (two copies).
-template <int D>
+// give the tiles of its strips (one contiguous copy each), ATTN phases the 32-key tiles of its unit (K and V
+// as swizzled tensor boxes).
+template <int D, int G>
 struct StepCursor {
   const StepArgs *A;
   int p, nphase, L, vk, P, npos;
   int kind;  // 0: between phases, 1: GEMV strips, 2: attention tiles
   const unsigned char *src;
   int nq, u, u1, q0;
-  const __half *kc, *vc;
-  int t, t1;
+  const CUtensorMap *km, *vm;  // the unit's layer's K and V cache maps
+  int hk, t, t1, l_;
 
   __device__ void init(const StepArgs &a, int vk_, int P_, int npos_) {
     A = &a;
@@ -290,14 +298,18 @@ struct StepCursor {
     npos = npos_;
     kind = 0;
   }
-  // The next stage's copies: (a, ba) and, for attention, (b, bb); false after the last stage.
-  __device__ bool next(const void *&a, uint32_t &ba, const void *&b, uint32_t &bb) {
+  // The next stage: a GEMV tile (a, ba), an attention tile of contiguous rows (K rows at a, V rows at b,
+  // ba = bb bytes each; GQA groups of 1 and 2) or an attention tile of tensor boxes (keys [y, y + 32) of KV head
+  // z in kmap and vmap, ba bytes in all; GQA groups of 4 and 8); false after the last stage.
+  __device__ bool next(const void *&a, uint32_t &ba, const void *&b, uint32_t &bb, const CUtensorMap *&kmap,
+                       const CUtensorMap *&vmap, int &y, int &z) {
     for (;;) {
       if (kind == 1 && u < u1) {
         a = src + ((int64_t)u * nq + q0) * kQ4QuadBytes;
         ba = (uint32_t)min(kQ4TileQuads, nq - q0) * kQ4QuadBytes;
         b = nullptr;
         bb = 0;
+        kmap = vmap = nullptr;
         q0 += kQ4TileQuads;
         if (q0 >= nq) {
           q0 = 0;
@@ -306,10 +318,22 @@ struct StepCursor {
         return true;
       }
       if (kind == 2 && t < t1) {
-        const int nk = min(kKeysPerTile, npos - t * kKeysPerTile);
-        a = kc + (int64_t)t * kKeysPerTile * D;
-        b = vc + (int64_t)t * kKeysPerTile * D;
-        ba = bb = (uint32_t)nk * D * 2;
+        if constexpr (kMmaAttn<G>) {
+          a = b = nullptr;
+          ba = 2u * (D / 64) * kBoxBytes;  // whole boxes land, keys past the cache included (as zeros)
+          bb = 0;
+          kmap = km;
+          vmap = vm;
+          y = t * kKeysPerTile;
+          z = hk;
+        } else {
+          const int nk = min(kKeysPerTile, npos - t * kKeysPerTile);
+          const int64_t off = ((int64_t)hk * A->cap + (int64_t)t * kKeysPerTile) * D;
+          a = A->layers[l_].k + off;
+          b = A->layers[l_].v + off;
+          ba = bb = (uint32_t)nk * D * 2;
+          kmap = vmap = nullptr;
+        }
         ++t;
         return true;
       }
@@ -320,11 +344,13 @@ struct StepCursor {
       if (ph == PH_ATTN) {
         const AttnSplit sp = attn_split(npos, A->Hkv, P);
         if (vk < sp.units) {
-          const int hk = vk / sp.S, s = vk % sp.S;
+          const int s = vk % sp.S;
+          hk = vk / sp.S;
           t = s * sp.nt / sp.S;
           t1 = (s + 1) * sp.nt / sp.S;
-          kc = A->layers[l].k + (int64_t)hk * A->cap * D;
-          vc = A->layers[l].v + (int64_t)hk * A->cap * D;
+          km = static_cast<const CUtensorMap *>(A->kv_maps) + 2 * l;
+          vm = km + 1;
+          l_ = l;
           kind = 2;
         }
       } else if (ph >= PH_QKV && ph <= PH_LM) {
@@ -346,16 +372,178 @@ struct StepCursor {
 
 // ---------------------------------------------------------------------------
 // Attention consumer: one unit (KV head hk, keys of tiles [t0, t1) + the
-// current key when `last`) on the 8 warps of a group.  Tile layout in a ring
-// slot: K rows [32][D] fp16, then V rows [32][D] fp16.  Warp w takes keys
-// [4w, 4w + 4) of every tile and keeps its own online softmax (running max,
-// sum and output in registers), so no group barrier runs inside a unit; the
-// eight warp states merge once at its end.
+// current key when `last`) on the 8 warps of a group, on tensor cores
+// (mma.sync m16n8k16, fp16 operands, fp32 accumulation).
+//
+// Ring slot layout (TMA tensor boxes, 128-byte swizzle): K as D/64 boxes of
+// [32 keys][64 dims] fp16, 4 KB each, then V the same way.  Row r of a box
+// holds its 16-byte chunk c at chunk position c ^ (r & 7), so the eight rows
+// of an ldmatrix 8x8 block sit in eight different bank groups.  Rows past the
+// tile's valid keys hold other cache positions (or zeros past the cache):
+// their scores are masked and their V entries zeroed in registers.
+//
+// Warp w takes key block kb = w & 1 (keys 16 kb .. 16 kb + 15 of every tile)
+// and output dims [dset D/4, (dset + 1) D/4), dset = w >> 1.  Per tile:
+//   S^T[16 keys][8 g] = K_kb q^T   (A = K rows by ldmatrix, B = q fragments,
+//                                   q = qh + ql as two fp16 halves, two MMAs
+//                                   per 16 dims: q keeps ~22 bits)
+//   online softmax per g over the warp's keys (running max, per-lane partial
+//   sums reduced once at the end);
+//   O^T[dims][g] += V^T[dims][16 keys] P^T (A = V rows by ldmatrix.trans,
+//                                   B = P^T by movmatrix; P = ph + pl, two MMAs)
+// The four warps of a key block compute the same scores and softmax state, so
+// the unit ends with a two-way merge (kb 0, kb 1) per output dim.  Columns
+// g >= G are padding (q = 0) and are never stored.
 // ---------------------------------------------------------------------------
 constexpr int r4(int x) { return (x + 3) & ~3; }
 
 template <int D, int G>
-struct AttnCfg {
+struct AttnCfgM {
+  static_assert(D == 64 || D == 128, "head_dim");
+  static_assert(G == 1 || G == 2 || G == 4 || G == 8, "GQA group");
+  static constexpr int NCH = D / 16;   // 16-dim chunks of a key row
+  static constexpr int NPC = NCH / 4;  // chunks of output dims per warp
+  static constexpr int NB = D / 64;    // boxes per K (or V) tile
+  // shared scratch (floats): q fragments [NCH][32 lanes][4 words], warp states (m, l) [8 warps][8 g][2],
+  // o [2 kb][G][D], and this step's key as a one-key tile in the ring layout with 16-row boxes (K, then V)
+  static constexpr int SM_QF = 0, SM_ML = NCH * 32 * 4, SM_O = SM_ML + 8 * 8 * 2, SM_KV = r4(SM_O + 2 * G * D),
+                       SM_END = SM_KV + 2 * NB * (kBoxBytes / 2) / 4;
+};
+static_assert(2 * 2 * kBoxBytes <= kQ4TileBytes, "attention tile fits a ring slot");
+
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ uint32_t movm_t(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+               "{%0,%1,%2,%3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+// Shared-memory address of 16-byte chunk cc (dims 8 cc .. 8 cc + 7) of row `row` of a tile of 128-byte rows in
+// boxes of `box` bytes (64 dims per box, 128-byte swizzle).
+__device__ __forceinline__ uint32_t swz_chunk(uint32_t tile, int box, int row, int cc) {
+  return tile + (uint32_t)((cc >> 3) * box + row * 128 + (((cc & 7) ^ (row & 7)) << 4));
+}
+
+// A warp's running state: max and per-lane partial sum of its two g columns, O^T fragments of its dims.
+template <int D, int G>
+struct WarpAttnM {
+  float m[2], l[2];
+  float o[AttnCfgM<D, G>::NPC][4];
+};
+
+template <int D, int G>
+__device__ __forceinline__ void attn_warp_init_m(WarpAttnM<D, G> &W) {
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    W.m[j] = -INFINITY;
+    W.l[j] = 0.0f;
+  }
+#pragma unroll
+  for (int c = 0; c < AttnCfgM<D, G>::NPC; ++c)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) W.o[c][j] = 0.0f;
+}
+
+// One tile for warp w: key block kb = w & 1 of the K tile at ktile and the V tile at vtile (shared-memory
+// addresses, boxes of `box` bytes), nk valid keys.
+template <int D, int G>
+__device__ __forceinline__ void attn_mma_tile(uint32_t ktile, uint32_t vtile, int box, int nk, const uint4 *qf,
+                                              WarpAttnM<D, G> &W, int w, int lane) {
+  using C = AttnCfgM<D, G>;
+  const int kb = w & 1, dset = w >> 1;
+  const int mi = lane >> 3, r8 = lane & 7;
+  // ---- scores S^T of keys 16 kb + (lane / 4, + 8), columns g = 2 (lane % 4) + (0, 1)
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  {
+    const int row = kb * 16 + r8 + (mi & 1) * 8;
+#pragma unroll
+    for (int ch = 0; ch < C::NCH; ++ch) {
+      uint32_t a[4];
+      ldsm_x4(a, swz_chunk(ktile, box, row, 2 * ch + (mi >> 1)));
+      const uint4 q = qf[ch * 32 + lane];
+      mma_f16(s, a, q.x, q.y);
+      mma_f16(s, a, q.z, q.w);
+    }
+  }
+  const int key0 = kb * 16 + (lane >> 2);
+  const bool v0 = key0 < nk, v1 = key0 + 8 < nk;
+  const float sv[4] = {v0 ? s[0] : -INFINITY, v0 ? s[1] : -INFINITY, v1 ? s[2] : -INFINITY, v1 ? s[3] : -INFINITY};
+  float tm[2] = {fmaxf(sv[0], sv[2]), fmaxf(sv[1], sv[3])};
+#pragma unroll
+  for (int o = 4; o < 32; o <<= 1)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) tm[j] = fmaxf(tm[j], __shfl_xor_sync(0xffffffffu, tm[j], o));
+  float al[2], p[4];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float mn = fmaxf(W.m[j], tm[j]);
+    al[j] = mn == -INFINITY ? 1.0f : expf(W.m[j] - mn);
+    p[j] = sv[j] == -INFINITY ? 0.0f : expf(sv[j] - mn);
+    p[j + 2] = sv[j + 2] == -INFINITY ? 0.0f : expf(sv[j + 2] - mn);
+    W.l[j] = W.l[j] * al[j] + (p[j] + p[j + 2]);
+    W.m[j] = mn;
+  }
+  // ---- P^T as the B operand: fp16 hi and lo parts, rows = keys turned into columns by movmatrix
+  const uint32_t h0 = pack_h2(p[0], p[1]), h1 = pack_h2(p[2], p[3]);
+  const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&h0));
+  const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&h1));
+  const uint32_t l0 = pack_h2(p[0] - f0.x, p[1] - f0.y), l1 = pack_h2(p[2] - f1.x, p[3] - f1.y);
+  const uint32_t bh0 = movm_t(h0), bh1 = movm_t(h1), bl0 = movm_t(l0), bl1 = movm_t(l1);
+  // ---- O^T += V^T P^T over this warp's dims
+  const int vrow = kb * 16 + r8 + (mi >> 1) * 8;
+  const int kc = kb * 16 + 2 * (lane & 3);  // keys of this lane's A elements: kc, kc + 1 (a0, a1), + 8 (a2, a3)
+  const bool partial = nk < 32;
+#pragma unroll
+  for (int c = 0; c < C::NPC; ++c) {
+    uint32_t a[4];
+    ldsm_x4_t(a, swz_chunk(vtile, box, vrow, 2 * (dset * C::NPC + c) + (mi & 1)));
+    if (partial) {  // rows past the valid keys: zero their V entries (p is 0 there, but 0 * inf is not)
+      const uint32_t m01 = (kc < nk ? 0x0000FFFFu : 0u) | (kc + 1 < nk ? 0xFFFF0000u : 0u);
+      const uint32_t m23 = (kc + 8 < nk ? 0x0000FFFFu : 0u) | (kc + 9 < nk ? 0xFFFF0000u : 0u);
+      a[0] &= m01;
+      a[1] &= m01;
+      a[2] &= m23;
+      a[3] &= m23;
+    }
+    W.o[c][0] *= al[0];
+    W.o[c][1] *= al[1];
+    W.o[c][2] *= al[0];
+    W.o[c][3] *= al[1];
+    mma_f16(W.o[c], a, bh0, bh1);
+    mma_f16(W.o[c], a, bl0, bl1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Attention consumer for GQA groups of 1 and 2 (CUDA cores): one unit on the
+// 8 warps of a group; ring slot = K rows [32][D] fp16 then V rows [32][D]
+// fp16, contiguous (one bulk copy each).  Warp w takes keys [4w, 4w + 4) of
+// every tile and keeps its own online softmax (running max, sum and output
+// in registers), so no group barrier runs inside a unit; the eight warp
+// states merge once at its end.  With one or two query rows per KV head the
+// tensor-core tile below would leave 7 or 6 of its 8 columns empty; this
+// path issues fewer instructions per key there.
+// ---------------------------------------------------------------------------
+template <int D, int G>
+struct AttnCfgS {
   static_assert(D == 64 || D == 128, "head_dim");
   static_assert(G == 1 || G == 2 || G == 4 || G == 8, "GQA group");
   static constexpr int NV = D / 64;              // q.k: lane 8 kk + c takes 16-byte chunks c + 8 v (v < NV) of key kk
@@ -376,8 +564,8 @@ __device__ __forceinline__ int q_swz(int dd) {
 }
 
 template <int D, int G>
-struct WarpAttn {
-  using C = AttnCfg<D, G>;
+struct WarpAttnS {
+  using C = AttnCfgS<D, G>;
   float q[C::QREG ? G * C::NV * 8 : 1];  // q[g][chunk c + 8 v][e] of this lane
   float m, l;                           // running max and sum of this lane's g (= c / GL)
   float o[G][C::DL];                    // output dims [DL lane, DL lane + DL) of every g
@@ -385,8 +573,8 @@ struct WarpAttn {
 
 // q element e of chunk (c + 8 v) of row g, read from shared memory (swizzled) or this lane's registers.
 template <int D, int G>
-__device__ __forceinline__ void attn_q8(const WarpAttn<D, G> &W, const float *sq, int g, int v, int c, float (&qv)[8]) {
-  using C = AttnCfg<D, G>;
+__device__ __forceinline__ void attn_q8s(const WarpAttnS<D, G> &W, const float *sq, int g, int v, int c, float (&qv)[8]) {
+  using C = AttnCfgS<D, G>;
   if constexpr (C::QREG) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) qv[e] = W.q[(g * C::NV + v) * 8 + e];
@@ -399,8 +587,8 @@ __device__ __forceinline__ void attn_q8(const WarpAttn<D, G> &W, const float *sq
 }
 
 template <int D, int G>
-__device__ __forceinline__ void attn_warp_init(WarpAttn<D, G> &W, const float *sq, int lane) {
-  using C = AttnCfg<D, G>;
+__device__ __forceinline__ void attn_warp_init_s(WarpAttnS<D, G> &W, const float *sq, int lane) {
+  using C = AttnCfgS<D, G>;
   if constexpr (C::QREG) {
     const int c = lane & 7;
 #pragma unroll
@@ -427,8 +615,8 @@ __device__ __forceinline__ void attn_warp_init(WarpAttn<D, G> &W, const float *s
 // other CTAs of this launch (read through L2).  sp: this warp's p / alpha exchange area (G >= 4).
 template <int D, int G, bool GLB>
 __device__ __forceinline__ void attn_warp_tile(const __half *kt, const __half *vt, int nk, const float *sq, float *sp,
-                                               WarpAttn<D, G> &W, int w, int lane) {
-  using C = AttnCfg<D, G>;
+                                               WarpAttnS<D, G> &W, int w, int lane) {
+  using C = AttnCfgS<D, G>;
   const int kk = lane >> 3, c = lane & 7, j = 4 * w + kk;
   const bool valid = j < nk;
   // ---- partial dots of this lane's chunks for every g (two chains each)
@@ -453,7 +641,7 @@ __device__ __forceinline__ void attn_warp_tile(const __half *kt, const __half *v
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       float qv[8];
-      attn_q8<D, G>(W, sq, g, v, c, qv);
+      attn_q8s<D, G>(W, sq, g, v, c, qv);
 #pragma unroll
       for (int e = 0; e < 8; e += 2) {
         sa[g] = fmaf(qv[e], kf[e], sa[g]);
@@ -552,6 +740,9 @@ __device__ __forceinline__ void attn_warp_tile(const __half *kt, const __half *v
   }
 }
 
+template <int D, int G>
+using AttnCfg = typename std::conditional<kMmaAttn<G>, AttnCfgM<D, G>, AttnCfgS<D, G>>::type;
+
 }  // namespace
 
 // ---------------------------------------------------------------------------
@@ -562,7 +753,7 @@ __device__ __forceinline__ void attn_warp_tile(const __half *kt, const __half *v
 template <int D, int G, bool TP>
 __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_constant__ StepArgs A) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
-  unsigned char *base = smem_raw + ((128 - (smem_u32(smem_raw) & 127)) & 127);
+  unsigned char *base = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);  // swizzled boxes: 1 KB
   __shared__ __align__(8) uint64_t full[kStepGroups][kStepStages], empty[kStepGroups][kStepStages];
   __shared__ float s_sum[(kStepConsumers / 32)];
   __shared__ int s_last[kStepGroups];
@@ -607,19 +798,29 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
     unsigned char *ring = rings + grp * kStepStages * kQ4TileBytes;
     uint64_t *fl = full[grp], *em = empty[grp];
     const uint64_t pol = l2_evict_first_policy();
-    StepCursor<D> ld;
+    StepCursor<D, G> ld;
     ld.init(A, vk, P, npos);
     const void *a, *b;
     uint32_t ba, bb;
+    const CUtensorMap *kmap, *vmap;
+    int y = 0, z = 0;
     int i = 0;
-    while (ld.next(a, ba, b, bb)) {
+    while (ld.next(a, ba, b, bb, kmap, vmap, y, z)) {
       const int st = i % kStepStages;
       if (i >= kStepStages && !mbar_wait(&em[st], (uint32_t)(i / kStepStages - 1) & 1, A.err, DEVERR_GEMV_EMPTY))
         break;
       unsigned char *slot = ring + st * kQ4TileBytes;
       mbar_arrive_expect_tx(&fl[st], ba + bb);
-      bulk_g2s(slot, a, ba, &fl[st], pol);
-      if (bb) bulk_g2s(slot + kKeysPerTile * D * 2, b, bb, &fl[st], pol);
+      if (!kmap) {
+        bulk_g2s(slot, a, ba, &fl[st], pol);
+        if (bb) bulk_g2s(slot + kKeysPerTile * D * 2, b, bb, &fl[st], pol);
+      } else {
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx) {
+          tma_load_3d(slot + bx * kBoxBytes, kmap, 64 * bx, y, z, &fl[st], pol);
+          tma_load_3d(slot + (D / 64 + bx) * kBoxBytes, vmap, 64 * bx, y, z, &fl[st], pol);
+        }
+      }
       ++i;
     }
     drain_ring<kStepStages>(fl, i, A.err);
@@ -661,71 +862,168 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
         const int hk = vk / sp.S, s = vk % sp.S;
         const int t0 = s * sp.nt / sp.S, t1 = (s + 1) * sp.nt / sp.S;
         const bool last = s == sp.S - 1;
-        for (int e = gtid; e < G * D; e += kGroupThreads)
-          sm[Cf::SM_Q + (e / D) * D + q_swz(e % D)] = __ldcg(A.q + (int64_t)hk * G * D + e) * A.scale;
-        if (last && gtid < D / 4) {  // key npos (written by this launch's QKV phase): K then V row, 16 B each
-          const int64_t row = ((int64_t)hk * A.cap + npos) * D;
-          const __half *src = (gtid < D / 8 ? s_layer[l & 1].k : s_layer[l & 1].v) + row + (gtid % (D / 8)) * 8;
-          reinterpret_cast<uint4 *>(sm + Cf::SM_KV)[gtid] = __ldcg(reinterpret_cast<const uint4 *>(src));
-        }
-        named_sync_id(gbar, kGroupThreads);
-        WarpAttn<D, G> W;
-        attn_warp_init<D, G>(W, sm + Cf::SM_Q, lane);
-        float *wp = sm + Cf::SM_P + gw * G * 5;
-        for (int t = t0; t < t1; ++t, ++i) {
-          const int sl = i % kStepStages;
-          ok = ok && mbar_wait(&fl[sl], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
-          if (ok) {
-            const __half *kt = reinterpret_cast<const __half *>(ring + sl * kQ4TileBytes);
-            attn_warp_tile<D, G, false>(kt, kt + kKeysPerTile * D, min(kKeysPerTile, npos - t * kKeysPerTile),
-                                        sm + Cf::SM_Q, wp, W, gw, lane);
+        if constexpr (kMmaAttn<G>) {
+          // q fragments (the B operand of the scores): lane L of chunk ch holds the fp16 (hi, lo) pairs of
+          // q[g = L / 4] at dims ch 16 + 2 (L % 4) (+ 1) and + 8, times the softmax scale; rows g >= G are zero
+          uint4 *qf = reinterpret_cast<uint4 *>(sm + Cf::SM_QF);
+          for (int e = gtid; e < Cf::NCH * 32; e += kGroupThreads) {
+            const int ch = e >> 5, ln = e & 31, g = ln >> 2, k0 = ch * 16 + 2 * (ln & 3);
+            uint4 f = make_uint4(0u, 0u, 0u, 0u);
+            if (g < G) {
+              const float *qg = A.q + (int64_t)(hk * G + g) * D;
+              const float2 a = __ldcg(reinterpret_cast<const float2 *>(qg + k0));
+              const float2 b = __ldcg(reinterpret_cast<const float2 *>(qg + k0 + 8));
+              const float q0 = a.x * A.scale, q1 = a.y * A.scale, q2 = b.x * A.scale, q3 = b.y * A.scale;
+              f.x = pack_h2(q0, q1);
+              f.y = pack_h2(q2, q3);
+              const float2 h0 = __half22float2(*reinterpret_cast<const __half2 *>(&f.x));
+              const float2 h1 = __half22float2(*reinterpret_cast<const __half2 *>(&f.y));
+              f.z = pack_h2(q0 - h0.x, q1 - h0.y);
+              f.w = pack_h2(q2 - h1.x, q3 - h1.y);
+            }
+            qf[e] = f;
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&em[sl]);
-        }
-        if (last && gw == 0 && ok) {  // key npos: this step's K/V, staged with q
-          const __half *kv = reinterpret_cast<const __half *>(sm + Cf::SM_KV);
-          attn_warp_tile<D, G, false>(kv, kv + D, 1, sm + Cf::SM_Q, wp, W, 0, lane);
-        }
-        // ---- merge the eight warp states into the unit's (m, l, o)
-        float *wml = sm + Cf::SM_ML, *wo = sm + Cf::SM_O;
-        {
-          const int c = lane & 7;
-          if (lane < 8 && c % Cf::GL == 0) {
-            wml[(gw * G + c / Cf::GL) * 2] = W.m;
-            wml[(gw * G + c / Cf::GL) * 2 + 1] = W.l;
+          const uint32_t kv1 = smem_u32(sm + Cf::SM_KV);  // the one-key tile: K boxes, then V boxes, 16 rows each
+          if (last && gtid < D / 4) {  // key npos (written by this launch's QKV phase) into row 0 (unswizzled)
+            const int64_t row = ((int64_t)hk * A.cap + npos) * D;
+            const int kv = gtid / (D / 8), cc = gtid % (D / 8);
+            const __half *src = (kv == 0 ? s_layer[l & 1].k : s_layer[l & 1].v) + row + cc * 8;
+            const uint32_t dst = swz_chunk(kv1 + kv * Cf::NB * (kBoxBytes / 2), kBoxBytes / 2, 0, cc);
+            const uint4 val = __ldcg(reinterpret_cast<const uint4 *>(src));
+            asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst), "r"(val.x), "r"(val.y), "r"(val.z),
+                         "r"(val.w)
+                         : "memory");
           }
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            float *dst = wo + (gw * G + g) * D + lane * Cf::DL;
-            if constexpr (Cf::DL == 4)
-              *reinterpret_cast<float4 *>(dst) = make_float4(W.o[g][0], W.o[g][1], W.o[g][2], W.o[g][3]);
-            else
-              *reinterpret_cast<float2 *>(dst) = make_float2(W.o[g][0], W.o[g][1]);
+          named_sync_id(gbar, kGroupThreads);
+          WarpAttnM<D, G> W;
+          attn_warp_init_m<D, G>(W);
+          for (int t = t0; t < t1; ++t, ++i) {
+            const int sl = i % kStepStages;
+            ok = ok && mbar_wait(&fl[sl], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
+            if (ok) {
+              const uint32_t kt = smem_u32(ring + sl * kQ4TileBytes);
+              attn_mma_tile<D, G>(kt, kt + Cf::NB * kBoxBytes, kBoxBytes, min(kKeysPerTile, npos - t * kKeysPerTile),
+                                  qf, W, gw, lane);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&em[sl]);
           }
-        }
-        named_sync_id(gbar, kGroupThreads);
-        float *part = A.attn_part + ((int64_t)hk * sp.S + s) * G * (D + 2);
-        for (int e = gtid; e < G * D; e += kGroupThreads) {
-          const int g = e / D, c = e % D;
-          float M = -INFINITY;
-#pragma unroll
-          for (int w = 0; w < kGroupWarps; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
-          float Ls = 0.0f, O = 0.0f;
-#pragma unroll
-          for (int w = 0; w < kGroupWarps; ++w) {
-            const float mw = wml[(w * G + g) * 2];
-            const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
-            Ls = fmaf(wml[(w * G + g) * 2 + 1], f, Ls);
-            O = fmaf(wo[(w * G + g) * D + c], f, O);
+          if (last && (gw & 1) == 0 && ok)  // key npos: the one-key tile, on the key-block-0 warps
+            attn_mma_tile<D, G>(kv1, kv1 + Cf::NB * (kBoxBytes / 2), kBoxBytes / 2, 1, qf, W, gw, lane);
+          // ---- merge the two key blocks' states into the unit's (m, l, o)
+          float *wml = sm + Cf::SM_ML, *wo = sm + Cf::SM_O;
+          {
+            float lt[2] = {W.l[0], W.l[1]};
+  #pragma unroll
+            for (int o = 4; o < 32; o <<= 1)
+  #pragma unroll
+              for (int j = 0; j < 2; ++j) lt[j] += __shfl_xor_sync(0xffffffffu, lt[j], o);
+            const int g0 = 2 * (lane & 3);
+            if (lane < 4) {
+              wml[(gw * 8 + g0) * 2] = W.m[0];
+              wml[(gw * 8 + g0) * 2 + 1] = lt[0];
+              wml[(gw * 8 + g0 + 1) * 2] = W.m[1];
+              wml[(gw * 8 + g0 + 1) * 2 + 1] = lt[1];
+            }
+            const int kb = gw & 1, dset = gw >> 1;
+  #pragma unroll
+            for (int c = 0; c < Cf::NPC; ++c) {
+              const int d0 = (dset * Cf::NPC + c) * 16 + (lane >> 2);
+  #pragma unroll
+              for (int j = 0; j < 2; ++j)
+                if (g0 + j < G) {
+                  wo[(kb * G + g0 + j) * D + d0] = W.o[c][j];
+                  wo[(kb * G + g0 + j) * D + d0 + 8] = W.o[c][2 + j];
+                }
+            }
           }
-          if (sp.S == 1) {
-            A.att[(int64_t)(hk * G + g) * D + c] = O / fmaxf(Ls, 1e-12f);
-          } else {
-            part[g * (D + 2) + 2 + c] = O;
-            if (c == 0) {
-              part[g * (D + 2)] = M;
-              part[g * (D + 2) + 1] = Ls;
+          named_sync_id(gbar, kGroupThreads);
+          float *part = A.attn_part + ((int64_t)hk * sp.S + s) * G * (D + 2);
+          for (int e = gtid; e < G * D; e += kGroupThreads) {
+            const int g = e / D, c = e % D, w0 = 2 * (c / (D / 4));
+            const float m0 = wml[(w0 * 8 + g) * 2], l0 = wml[(w0 * 8 + g) * 2 + 1];
+            const float m1 = wml[((w0 + 1) * 8 + g) * 2], l1 = wml[((w0 + 1) * 8 + g) * 2 + 1];
+            const float M = fmaxf(m0, m1);
+            const float f0 = m0 == -INFINITY ? 0.0f : expf(m0 - M), f1 = m1 == -INFINITY ? 0.0f : expf(m1 - M);
+            const float Ls = fmaf(l1, f1, l0 * f0);
+            const float O = fmaf(wo[(G + g) * D + c], f1, wo[g * D + c] * f0);
+            if (sp.S == 1) {
+              A.att[(int64_t)(hk * G + g) * D + c] = O / fmaxf(Ls, 1e-12f);
+            } else {
+              part[g * (D + 2) + 2 + c] = O;
+              if (c == 0) {
+                part[g * (D + 2)] = M;
+                part[g * (D + 2) + 1] = Ls;
+              }
+            }
+          }
+        } else {
+          for (int e = gtid; e < G * D; e += kGroupThreads)
+            sm[Cf::SM_Q + (e / D) * D + q_swz(e % D)] = __ldcg(A.q + (int64_t)hk * G * D + e) * A.scale;
+          if (last && gtid < D / 4) {  // key npos (written by this launch's QKV phase): K then V row, 16 B each
+            const int64_t row = ((int64_t)hk * A.cap + npos) * D;
+            const __half *src = (gtid < D / 8 ? s_layer[l & 1].k : s_layer[l & 1].v) + row + (gtid % (D / 8)) * 8;
+            reinterpret_cast<uint4 *>(sm + Cf::SM_KV)[gtid] = __ldcg(reinterpret_cast<const uint4 *>(src));
+          }
+          named_sync_id(gbar, kGroupThreads);
+          WarpAttnS<D, G> W;
+          attn_warp_init_s<D, G>(W, sm + Cf::SM_Q, lane);
+          float *wp = sm + Cf::SM_P + gw * G * 5;
+          for (int t = t0; t < t1; ++t, ++i) {
+            const int sl = i % kStepStages;
+            ok = ok && mbar_wait(&fl[sl], (uint32_t)(i / kStepStages) & 1, A.err, DEVERR_GEMV_FULL);
+            if (ok) {
+              const __half *kt = reinterpret_cast<const __half *>(ring + sl * kQ4TileBytes);
+              attn_warp_tile<D, G, false>(kt, kt + kKeysPerTile * D, min(kKeysPerTile, npos - t * kKeysPerTile),
+                                          sm + Cf::SM_Q, wp, W, gw, lane);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&em[sl]);
+          }
+          if (last && gw == 0 && ok) {  // key npos: this step's K/V, staged with q
+            const __half *kv = reinterpret_cast<const __half *>(sm + Cf::SM_KV);
+            attn_warp_tile<D, G, false>(kv, kv + D, 1, sm + Cf::SM_Q, wp, W, 0, lane);
+          }
+          // ---- merge the eight warp states into the unit's (m, l, o)
+          float *wml = sm + Cf::SM_ML, *wo = sm + Cf::SM_O;
+          {
+            const int c = lane & 7;
+            if (lane < 8 && c % Cf::GL == 0) {
+              wml[(gw * G + c / Cf::GL) * 2] = W.m;
+              wml[(gw * G + c / Cf::GL) * 2 + 1] = W.l;
+            }
+  #pragma unroll
+            for (int g = 0; g < G; ++g) {
+              float *dst = wo + (gw * G + g) * D + lane * Cf::DL;
+              if constexpr (Cf::DL == 4)
+                *reinterpret_cast<float4 *>(dst) = make_float4(W.o[g][0], W.o[g][1], W.o[g][2], W.o[g][3]);
+              else
+                *reinterpret_cast<float2 *>(dst) = make_float2(W.o[g][0], W.o[g][1]);
+            }
+          }
+          named_sync_id(gbar, kGroupThreads);
+          float *part = A.attn_part + ((int64_t)hk * sp.S + s) * G * (D + 2);
+          for (int e = gtid; e < G * D; e += kGroupThreads) {
+            const int g = e / D, c = e % D;
+            float M = -INFINITY;
+  #pragma unroll
+            for (int w = 0; w < kGroupWarps; ++w) M = fmaxf(M, wml[(w * G + g) * 2]);
+            float Ls = 0.0f, O = 0.0f;
+  #pragma unroll
+            for (int w = 0; w < kGroupWarps; ++w) {
+              const float mw = wml[(w * G + g) * 2];
+              const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+              Ls = fmaf(wml[(w * G + g) * 2 + 1], f, Ls);
+              O = fmaf(wo[(w * G + g) * D + c], f, O);
+            }
+            if (sp.S == 1) {
+              A.att[(int64_t)(hk * G + g) * D + c] = O / fmaxf(Ls, 1e-12f);
+            } else {
+              part[g * (D + 2) + 2 + c] = O;
+              if (c == 0) {
+                part[g * (D + 2)] = M;
+                part[g * (D + 2) + 1] = Ls;
+              }
             }
           }
         }
@@ -967,7 +1265,7 @@ size_t decode_step_xarea(int d, int G, int64_t H, int64_t I, int64_t qdim) {
 }
 
 size_t decode_step_smem(int d, int G, int64_t H, int64_t I, int64_t qdim) {
-  return 128 + (size_t)kStepGroups * kStepStages * kQ4TileBytes + decode_step_xarea(d, G, H, I, qdim) +
+  return 1024 + (size_t)kStepGroups * kStepStages * kQ4TileBytes + decode_step_xarea(d, G, H, I, qdim) +
          (size_t)kStepGroups * 2 * kGroupWarps * kQ4StripRows * 4;
 }
 

@@ -29,6 +29,7 @@
 
 #include "q4_gemv.cuh"
 #include "runtime.cuh"
+#include "tmap.cuh"
 
 using namespace fg;
 
@@ -446,6 +447,20 @@ void setup_step(fg_llama *m) {
   A.gs = c.gemv;
   A.err = c.gemv.err;
   A.xarea_bytes = decode_step_xarea(d, G, m->H, m->I_l, (int64_t)m->Hq_l * d);
+  {  // tensor maps of the K and V caches (the step kernel's attention tiles: 32 keys x 64 dims per box)
+    std::vector<CUtensorMap> maps(2 * std::max(L, 1));
+    for (int l = 0; l < L; ++l) {
+      const LayerW &w = m->layers[l];
+      for (int kv = 0; kv < 2; ++kv)
+        maps[2 * l + kv] = make_tmap_3d(kv ? (const void *)w.v : (const void *)w.k, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                                        (uint64_t)d, (uint64_t)m->cap, (uint64_t)m->Hkv_l, (uint64_t)d * 2,
+                                        (uint64_t)m->cap * d * 2, 64, 32, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+    }
+    void *dm = m->dalloc(sizeof(CUtensorMap) * maps.size());
+    FG_REQUIRE(((uintptr_t)dm & 63) == 0, FG_ERR_DEVICE, "decode step: tensor maps must be 64-byte aligned");
+    c.h2d(dm, maps.data(), sizeof(CUtensorMap) * maps.size());
+    A.kv_maps = dm;
+  }
   A.vocab_l = m->V_l;
   A.vbase = m->rank * m->V_l;
   A.tp = m->tp;

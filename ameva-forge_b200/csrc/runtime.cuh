@@ -269,6 +269,9 @@ struct StepArgs {
   unsigned long long *bar;     // grid barrier arrivals, launches; attention arrivals per head so far (never reset)
   int *err;
   uint64_t xarea_bytes;
+  // [L][2] CUtensorMap of every layer's K and V cache ([Hkv][cap][d] fp16, boxes of 32 keys x 64 dims, 128-byte
+  // swizzle): the attention phases' tile copies
+  const void *kv_maps = nullptr;
   // tensor parallelism (tp > 1): rank r's exchange region at xr[r] (a peer mapping for r != rank):
   // float part[2][tp][H] (partial sums of o_proj / down_proj by source rank, by exchange parity),
   // then at byte xflags: u64 pflag[8] (exchange sequence per source), u64 key[8], u64 kflag[8].

@@ -18,6 +18,8 @@ pytestmark = pytest.mark.gpu
 
 TINY2 = dict(O.LlamaShape(32000, 2048, 5632, 2, 32, 4).__dict__)   # head_dim 64, GQA 8:1
 L7B1 = dict(O.LlamaShape(32000, 4096, 11008, 1, 32, 32).__dict__)  # head_dim 128, MHA
+GQA4 = dict(O.LlamaShape(32000, 4096, 11008, 1, 32, 8).__dict__)   # head_dim 128, GQA 4:1 (tensor-core tiles)
+GQA2 = dict(O.LlamaShape(32000, 2048, 5632, 1, 32, 16).__dict__)   # head_dim 64, GQA 2:1 (CUDA-core tiles)
 
 
 def make(ctx, shape, seed, cap, layered=False):
@@ -40,6 +42,9 @@ def make(ctx, shape, seed, cap, layered=False):
     ("tinyllama_2layer", TINY2, 300),   # 10 tiles of keys: 5 splits of two tiles per KV head
     ("llama7b_1layer", L7B1, 340),      # 11 tiles: 5 splits, the last of three tiles; partial last tile
     ("llama7b_1layer_short", L7B1, 5),  # one partial tile, one split
+    ("gqa4_d128_1layer", GQA4, 201),    # 7 tiles, the last partial
+    ("gqa4_d128_short", GQA4, 3),       # one partial tile
+    ("gqa2_d64_1layer", GQA2, 100),
 ])
 def test_step_kernel_equals_layered_decode(ctx, name, shape, plen):
     prompt = (np.arange(plen, dtype=np.int32) * 7919 % 32000).reshape(1, plen)
