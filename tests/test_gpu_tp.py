@@ -20,15 +20,20 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-SHAPE = dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
-             num_key_value_heads=2)
+# GQA 2:1 per rank (the step kernel's CUDA-core attention tile) and GQA 4:1 (its tensor-core tile)
+SHAPES = {
+    "gqa2": dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                 num_key_value_heads=2),
+    "gqa4": dict(vocab_size=512, hidden_size=512, intermediate_size=512, num_hidden_layers=2, num_attention_heads=8,
+                 num_key_value_heads=2),
+}
 SEED, STEPS = 97, 3
 PROMPT = ((np.arange(40, dtype=np.int32) * 37 + 11) % 512).reshape(1, 40)
 
 
-def _run(ctx, out_path):
+def _run(ctx, shape, out_path):
     import forge_b200
-    cfg = forge_b200.LlamaConfig(max_position_embeddings=64, max_batch=1, qtype="Q4_0", **SHAPE)
+    cfg = forge_b200.LlamaConfig(max_position_embeddings=64, max_batch=1, qtype="Q4_0", **SHAPES[shape])
     m = forge_b200.LlamaForCausalLM(cfg, ctx)
     m.synthesize(SEED)
     path = m.decode_path(1)
@@ -45,25 +50,26 @@ def _run(ctx, out_path):
         np.savez(out_path, logits=np.stack(seq), tokens=np.array(toks), path=np.array(path))
 
 
-def _rank(rank, world, nid, out_dir):
+def _rank(rank, world, nid, shape, out_dir):
     import forge_b200
     ctx = forge_b200.Context(device=rank, tp_rank=rank, tp_size=world, nccl_id=nid)
-    _run(ctx, os.path.join(out_dir, "tp2.npz") if rank == 0 else None)
+    _run(ctx, shape, os.path.join(out_dir, "tp2.npz") if rank == 0 else None)
     ctx.shutdown()
     if rank == 0:  # the unsharded model on the same device
         ctx1 = forge_b200.Context(device=0)
-        _run(ctx1, os.path.join(out_dir, "tp1.npz"))
+        _run(ctx1, shape, os.path.join(out_dir, "tp1.npz"))
         ctx1.shutdown()
 
 
-def test_two_gpu_tensor_parallel_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("shape", sorted(SHAPES))
+def test_two_gpu_tensor_parallel_matches_single_gpu(tmp_path, shape):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import forge_b200
     nid = forge_b200.nccl_unique_id()
-    ctxs = mp.start_processes(_rank, args=(2, nid, str(tmp_path)), nprocs=2, join=False, start_method="spawn")
+    ctxs = mp.start_processes(_rank, args=(2, nid, shape, str(tmp_path)), nprocs=2, join=False, start_method="spawn")
     deadline = time.time() + 240
     while not ctxs.join(timeout=5):
         if time.time() > deadline:
