@@ -629,7 +629,7 @@ void qmatmul_kquant(Ctx &c, const Tensor &xt, const Tensor &wt, int64_t M, float
   const int64_t N = wt.shape[0], K = wt.shape[1];
   if (M <= 8) {
     if (wt.dtype == FG_Q4_K)
-      launch_qmatmul_q4k(wt.ptr, N, K, (const float *)xt.ptr, M, y, nullptr, c.stream);
+      launch_qmatmul_q4k(wt.ptr, N, K, (const float *)xt.ptr, M, y, nullptr, c.gemv.err, c.stream);
     else
       launch_qmatmul_q6k(wt.ptr, N, K, (const float *)xt.ptr, M, y, nullptr, c.stream);
     return;

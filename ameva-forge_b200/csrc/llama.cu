@@ -177,7 +177,7 @@ void kq_linear(fg_llama *m, const KQ &w, const float *x, int M, float *y) {
              (long long)w.N, (long long)w.K);
   if (M <= 8) {
     if (w.type == FG_Q4_K)
-      launch_qmatmul_q4k(w.p, w.N, w.K, x, M, y, nullptr, c.stream);
+      launch_qmatmul_q4k(w.p, w.N, w.K, x, M, y, nullptr, c.gemv.err, c.stream);
     else
       launch_qmatmul_q6k(w.p, w.N, w.K, x, M, y, nullptr, c.stream);
     return;

@@ -21,7 +21,9 @@
 // super-blocks per stage (16-byte cp.async copies), so ~3.4 KB per warp are
 // in flight without holding registers.  HBM-bound: 144 bytes per 256 weights.  Larger M dequantises the
 // matrix once and runs the fp32 GEMM.
-#include "epilogue.cuh"
+#include <cstdlib>
+
+#include "q4_gemv.cuh"
 #include "runtime.cuh"
 #include "tma.cuh"
 
@@ -170,6 +172,253 @@ __global__ void __launch_bounds__(kQ4kWarps * 32) k_gemv_q4k(const uint8_t *__re
 template <int M>
 void gemv_q4k_launch(const uint8_t *w, int64_t N, int64_t K, const float *x, float *y, cudaStream_t s) {
   k_gemv_q4k<M><<<(unsigned)ceil_div(N, kQ4kWarps), kQ4kWarps * 32, kQ4kSmem, s>>>(w, N, K, x, K, y, N);
+  FG_LAUNCH_CHECK();
+}
+
+
+// ---------------------------------------------------------------------------
+// Q4_K GEMV on integer tensor cores (M <= 4 activation rows): the Q4_0
+// design (q4_gemv.cuh) on GGUF-ordered Q4_K rows.
+//  * Units are 16-row strips; a tile is 16 rows x 8 super-blocks, one bulk
+//    copy per row into a ring slot whose rows are 16 bytes apart beyond their
+//    1152 data bytes, so the 8 rows x 4 words an MMA fragment load touches
+//    fall in 32 different banks.
+//  * Warp w takes super-block w of a tile: sub-block j = 2c + h is nibble h of
+//    code bytes 32c .. 32c + 31, i.e. element k of the sub-block is nibble h
+//    of byte 32c + k -- the k order of the u8 A fragment of mma.sync
+//    m16n8k32, so each fragment register is a masked 32-bit load.
+//  * x is staged exactly as for Q4_0 (per-block power-of-two scale 2^e,
+//    22-bit integer v split into three s8 digits); the MMA input C is 0, so
+//    D = sum_k q_k digit_k.  A sub-block contributes
+//      2^-e (s * sum q v - o * sum v),  s = d * scale, o = dmin * min,
+//    with sum v per block and token taken from the staged digit sums.  Lane t
+//    decodes the (scale, min) pairs of sub-blocks 2t, 2t + 1 of its two rows
+//    (the byte permutes of q4k_pair) and the quad of lanes shares them by
+//    shuffles.
+// Bound: HBM, 144 bytes per 256 weights (+ x).
+// ---------------------------------------------------------------------------
+constexpr int kKmWarps = 8;                          // consumer warps
+constexpr int kKmThreads = (kKmWarps + 1) * 32;      // + the producer warp
+constexpr int kKmTileSb = 8;                         // super-blocks per tile row
+constexpr int kKmRowStride = kKmTileSb * 144 + 16;   // 1168: rows 4 banks apart
+constexpr int kKmTileBytes = 16 * kKmRowStride;      // 18688
+
+template <int MV>
+size_t q4k_mma_smem(int64_t K, int stages) {
+  const int nb = (int)(K / 32);
+  return 128 + (size_t)stages * kKmTileBytes + Q4X<MV>::bytes(nb) + (size_t)MV * nb * 4 +
+         (size_t)2 * kKmWarps * kQ4StripRows * MV * 4;
+}
+
+template <int MV, int STAGES>
+__global__ void __launch_bounds__(kKmThreads, 2)
+    k_gemv_q4k_mma(const uint8_t *__restrict__ w, int64_t N, int64_t K, const float *__restrict__ x, int64_t ldx,
+                   float *__restrict__ y, int64_t ldy, int *err) {
+  constexpr int NM = Q4X<MV>::NM;
+  extern __shared__ __align__(128) unsigned char km_smem[];
+  unsigned char *ring = km_smem + ((128 - (smem_u32(km_smem) & 127)) & 127);
+  __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
+  __shared__ float s_sum[kKmWarps * MV];
+  __shared__ float s_one[MV];
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nsb = (int)(K / 256), nb = nsb * 8;
+  const int ntile = (nsb + kKmTileSb - 1) / kKmTileSb;
+  const Sched sc = make_sched(N, kQ4StripRows, 1, blockIdx.x, gridDim.x);
+  Q4X<MV> X;
+  X.carve(ring + STAGES * kKmTileBytes, nb, nb);
+  float *fsv = reinterpret_cast<float *>(ring + STAGES * kKmTileBytes + Q4X<MV>::bytes(nb));  // [MV][nb]: sum v / 128
+  float *red = fsv + MV * nb;                                                                // [2][8][16][MV]
+
+  if (tid == 0) {
+    for (int st = 0; st < STAGES; ++st) {
+      mbar_init(&full[st], 1);
+      mbar_init(&empty[st], kKmWarps);
+    }
+    fence_barrier_init();
+  }
+  if (tid < MV) s_one[tid] = 1.0f;
+  __syncthreads();
+
+  if (warp == kKmWarps) {
+    // ---------------- producer: the tiles of strips [u0, u1), one bulk copy per row
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      int i = 0;
+      bool ok = true;
+      for (int u = sc.u0; u < sc.u1 && ok; ++u) {
+        const int nrows = (int)(N - (int64_t)u * kQ4StripRows < kQ4StripRows ? N - (int64_t)u * kQ4StripRows : kQ4StripRows);
+        for (int tl = 0; tl < ntile && ok; ++tl, ++i) {
+          const int st = i % STAGES;
+          if (i >= STAGES && !mbar_wait(&empty[st], (uint32_t)(i / STAGES - 1) & 1, err, DEVERR_GEMV_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const int nst = min(kKmTileSb, nsb - tl * kKmTileSb);
+          mbar_arrive_expect_tx(&full[st], (uint32_t)(nrows * nst * 144));
+          for (int r = 0; r < nrows; ++r)
+            bulk_g2s(ring + st * kKmTileBytes + r * kKmRowStride,
+                     w + (((int64_t)u * kQ4StripRows + r) * nsb + (int64_t)tl * kKmTileSb) * 144,
+                     (uint32_t)(nst * 144), &full[st], pol);
+        }
+      }
+      drain_ring<STAGES>(full, i, err);
+    }
+    return;
+  }
+
+  // ---------------- stage x; the blocks' digit sums for the min term
+  constexpr int kC = kKmWarps * 32;
+  q4_stage_x<MV>(X, x, ldx, nullptr, tid, kC, s_sum);
+  named_sync(kC);
+  for (int e = tid; e < MV * nb; e += kC) {
+    const int m = e / nb, b = e % nb;
+    // staged MMA offsets are -8 x (digit sums): sum v = 2^14 sum hi + 2^7 sum mid + sum lo
+    const int sv = -(X.cx0[(2 * m) * nb + b] * 16384 + X.cx1[(2 * m) * nb + b] * 128 + X.cx0[(2 * m + 1) * nb + b]) / 8;
+    fsv[e] = (float)sv * 0.0078125f;
+  }
+  named_sync(kC);
+
+  // ---------------- consume
+  Q4Lane<MV> L;
+  L.init(X, lane);
+  const int gq = lane >> 2, t = lane & 3;
+  const float evn = (t & 1) ? 0.0f : 1.0f;  // lanes of the (hi, mid) columns carry the min term
+  const float *fbp[NM], *fsp[NM];
+#pragma unroll
+  for (int im = 0; im < NM; ++im) {
+    const int tok = min(2 * im + (t >> 1), MV - 1);  // padding tokens' columns are dropped at the end
+    fbp[im] = X.fbk + tok * nb;
+    fsp[im] = fsv + tok * nb;
+  }
+  QMat wq;
+  wq.N = N;
+  Epilogue ep;
+  ep.mode = EPI_PLAIN;
+  ep.y = y;
+  ep.ldy = ldy;
+  float2 acc[NM];
+#pragma unroll
+  for (int im = 0; im < NM; ++im) acc[im] = make_float2(0.0f, 0.0f);
+  bool ok = true;
+  int i = 0;
+  for (int u = sc.u0; u < sc.u1; ++u) {
+    for (int tl = 0; tl < ntile; ++tl, ++i) {
+      const int st = i % STAGES;
+      ok = ok && mbar_wait(&full[st], (uint32_t)(i / STAGES) & 1, err, DEVERR_GEMV_FULL);
+      const int sbg = tl * kKmTileSb + warp;
+      if (ok && sbg < nsb) {
+        const unsigned char *r0 = ring + st * kKmTileBytes + gq * kKmRowStride + warp * 144, *r1 = r0 + 8 * kKmRowStride;
+        const uint4 h0 = *reinterpret_cast<const uint4 *>(r0), h1 = *reinterpret_cast<const uint4 *>(r1);
+        uint32_t sc0, mn0, sc1, mn1;
+        q4k_pair(h0, t, sc0, mn0);
+        q4k_pair(h1, t, sc1, mn1);
+        const float d0 = __half2float(__ushort_as_half((unsigned short)(h0.x & 0xFFFF)));
+        const float dm0 = __half2float(__ushort_as_half((unsigned short)(h0.x >> 16)));
+        const float d1 = __half2float(__ushort_as_half((unsigned short)(h1.x & 0xFFFF)));
+        const float dm1 = __half2float(__ushort_as_half((unsigned short)(h1.x >> 16)));
+        // [row][sub-block 2t + hh]: s = d * scale, o = dmin * min
+        const float sv0[2] = {d0 * (float)(sc0 & 0xFF), d0 * (float)(sc0 >> 8)};
+        const float ov0[2] = {dm0 * (float)(mn0 & 0xFF), dm0 * (float)(mn0 >> 8)};
+        const float sv1[2] = {d1 * (float)(sc1 & 0xFF), d1 * (float)(sc1 >> 8)};
+        const float ov1[2] = {dm1 * (float)(mn1 & 0xFF), dm1 * (float)(mn1 >> 8)};
+        const int b0 = sbg * 8;
+        float4 FB[NM][2], SV[NM][2];
+#pragma unroll
+        for (int im = 0; im < NM; ++im)
+#pragma unroll
+          for (int hf = 0; hf < 2; ++hf) {
+            FB[im][hf] = *reinterpret_cast<const float4 *>(fbp[im] + b0 + 4 * hf);
+            SV[im][hf] = *reinterpret_cast<const float4 *>(fsp[im] + b0 + 4 * hf);
+          }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t w00 = *reinterpret_cast<const uint32_t *>(r0 + 16 + 32 * c + 4 * t);
+          const uint32_t w01 = *reinterpret_cast<const uint32_t *>(r0 + 32 + 32 * c + 4 * t);
+          const uint32_t w10 = *reinterpret_cast<const uint32_t *>(r1 + 16 + 32 * c + 4 * t);
+          const uint32_t w11 = *reinterpret_cast<const uint32_t *>(r1 + 32 + 32 * c + 4 * t);
+          const int src = (lane & ~3) | c;  // the lane holding sub-blocks 2c, 2c + 1 of these rows
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int j = 2 * c + hh, b = b0 + j;
+            const float sa = __shfl_sync(0xffffffffu, sv0[hh], src), sb = __shfl_sync(0xffffffffu, sv1[hh], src);
+            const float oa = __shfl_sync(0xffffffffu, ov0[hh], src), ob = __shfl_sync(0xffffffffu, ov1[hh], src);
+            const uint32_t a0 = hh ? (w00 >> 4) & 0x0F0F0F0Fu : w00 & 0x0F0F0F0Fu;
+            const uint32_t a1 = hh ? (w10 >> 4) & 0x0F0F0F0Fu : w10 & 0x0F0F0F0Fu;
+            const uint32_t a2 = hh ? (w01 >> 4) & 0x0F0F0F0Fu : w01 & 0x0F0F0F0Fu;
+            const uint32_t a3 = hh ? (w11 >> 4) & 0x0F0F0F0Fu : w11 & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int im = 0; im < NM; ++im) {
+              uint2 B = make_uint2(0u, 0u);
+              if (L.xv[im]) B = L.xl[im][b * 3 * MV * 4];
+              int di[4];
+              imma_u8s8(di, a0, a1, a2, a3, B.x, B.y, 0, 0);
+              const float vx = (float)(di[0] * 128 + di[1]), vy = (float)(di[2] * 128 + di[3]);
+              const float4 &f4 = FB[im][j >> 2];
+              const float4 &s4 = SV[im][j >> 2];
+              const float fb = (j & 3) == 0 ? f4.x : (j & 3) == 1 ? f4.y : (j & 3) == 2 ? f4.z : f4.w;
+              const float sv = evn * ((j & 3) == 0 ? s4.x : (j & 3) == 1 ? s4.y : (j & 3) == 2 ? s4.z : s4.w);
+              const float2 r = make_float2(fmaf(sa, vx, -oa * sv), fmaf(sb, vy, -ob * sv));
+              acc[im] = ffma2(make_float2(fb, fb), r, acc[im]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    float *rb = red + ((u - sc.u0) & 1) * (kKmWarps * kQ4StripRows * MV);
+    q4_group_red<MV>(rb, acc, warp, lane);
+    named_sync(kC);
+    if (ok) finish_strip<MV>(wq, ep, u, rb, s_one, tid, kC);
+  }
+}
+
+int q4k_num_sms() {
+  static int sms[64] = {0};
+  int dev = 0;
+  FG_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return 148;
+  if (!sms[dev]) FG_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+  return sms[dev];
+}
+
+// Shared memory per CTA up to which two CTAs share an SM, and the most one CTA may take.
+constexpr size_t kKmSmemTwo = 112 * 1024, kKmSmemOne = 225 * 1024;
+
+// Ring depth: 4 stages, or 3 where only that keeps two CTAs per SM or fits one; 0: x of MV tokens does not
+// fit beside a 3-stage ring (the CUDA-core GEMV takes the call).
+template <int MV>
+int q4k_mma_stages(int64_t K) {
+  if (q4k_mma_smem<MV>(K, 4) <= kKmSmemTwo) return 4;
+  if (q4k_mma_smem<MV>(K, 3) <= kKmSmemTwo) return 3;
+  if (q4k_mma_smem<MV>(K, 4) <= kKmSmemOne) return 4;
+  return q4k_mma_smem<MV>(K, 3) <= kKmSmemOne ? 3 : 0;
+}
+
+template <int MV>
+void gemv_q4k_mma_launch(const uint8_t *w, int64_t N, int64_t K, const float *x, float *y, int *err,
+                         cudaStream_t s) {
+  const int stages = q4k_mma_stages<MV>(K);
+  if (!stages) return gemv_q4k_launch<MV>(w, N, K, x, y, s);
+  const size_t smem = q4k_mma_smem<MV>(K, stages);
+  const int64_t strips = q4_strips(N);
+  const int P = (int)std::min<int64_t>((smem <= kKmSmemTwo ? 2 : 1) * (int64_t)q4k_num_sms(), strips);
+  static unsigned long long attr_set[2] = {0, 0};  // per ring depth, one bit per device
+  int dev = 0;
+  FG_CUDA(cudaGetDevice(&dev));
+  const int inst = stages == 3 ? 1 : 0;
+  if (!(attr_set[inst] & (1ull << dev))) {
+    if (stages == 3)
+      FG_CUDA(cudaFuncSetAttribute(k_gemv_q4k_mma<MV, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kKmSmemOne));
+    else
+      FG_CUDA(cudaFuncSetAttribute(k_gemv_q4k_mma<MV, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kKmSmemOne));
+    attr_set[inst] |= 1ull << dev;
+  }
+  if (stages == 3)
+    k_gemv_q4k_mma<MV, 3><<<P, kKmThreads, smem, s>>>(w, N, K, x, K, y, N, err);
+  else
+    k_gemv_q4k_mma<MV, 4><<<P, kKmThreads, smem, s>>>(w, N, K, x, K, y, N, err);
   FG_LAUNCH_CHECK();
 }
 
@@ -326,16 +575,18 @@ void launch_dequant_q4k(const void *blocks, int64_t n_blocks, float *out, cudaSt
   FG_LAUNCH_CHECK();
 }
 
-// y[M, N] = x[M, K] W^T, W Q4_K [N, K]; `scratch` (N K floats) is used when M > 8.
+// y[M, N] = x[M, K] W^T, W Q4_K [N, K]; `scratch` (N K floats) is used when M > 8; `err` (the context's
+// device error word) takes the integer-MMA GEMV's wait timeouts (M <= 4; null: the CUDA-core GEMV).
 void launch_qmatmul_q4k(const void *w, int64_t N, int64_t K, const float *x, int64_t M, float *y, float *scratch,
-                        cudaStream_t s) {
+                        int *err, cudaStream_t s) {
   if (M == 0 || N == 0) return;
   const uint8_t *wb = (const uint8_t *)w;
+  const bool mma = err && ((uintptr_t)x & 15) == 0 && K % 256 == 0 && std::getenv("FORGE_B200_Q4K") == nullptr;
   switch (M) {
-    case 1: return gemv_q4k_launch<1>(wb, N, K, x, y, s);
-    case 2: return gemv_q4k_launch<2>(wb, N, K, x, y, s);
-    case 3: return gemv_q4k_launch<3>(wb, N, K, x, y, s);
-    case 4: return gemv_q4k_launch<4>(wb, N, K, x, y, s);
+    case 1: return mma ? gemv_q4k_mma_launch<1>(wb, N, K, x, y, err, s) : gemv_q4k_launch<1>(wb, N, K, x, y, s);
+    case 2: return mma ? gemv_q4k_mma_launch<2>(wb, N, K, x, y, err, s) : gemv_q4k_launch<2>(wb, N, K, x, y, s);
+    case 3: return mma ? gemv_q4k_mma_launch<3>(wb, N, K, x, y, err, s) : gemv_q4k_launch<3>(wb, N, K, x, y, s);
+    case 4: return mma ? gemv_q4k_mma_launch<4>(wb, N, K, x, y, err, s) : gemv_q4k_launch<4>(wb, N, K, x, y, s);
     case 5: return gemv_q4k_launch<5>(wb, N, K, x, y, s);
     case 6: return gemv_q4k_launch<6>(wb, N, K, x, y, s);
     case 7: return gemv_q4k_launch<7>(wb, N, K, x, y, s);

@@ -131,7 +131,7 @@ void launch_dequant(const QMat &w, float *out, cudaStream_t s);
 // q4k.cu: GGUF Q4_K / Q6_K (blocks in GGUF order, [N][K / 256] x 144 / 210 bytes)
 void launch_dequant_q4k(const void *blocks, int64_t n_blocks, float *out, cudaStream_t s);
 void launch_qmatmul_q4k(const void *w, int64_t N, int64_t K, const float *x, int64_t M, float *y, float *scratch,
-                        cudaStream_t s);
+                        int *err, cudaStream_t s);
 void launch_dequant_q6k(const void *blocks, int64_t n_blocks, float *out, cudaStream_t s);
 void launch_qmatmul_q6k(const void *w, int64_t N, int64_t K, const float *x, int64_t M, float *y, float *scratch,
                         cudaStream_t s);
