@@ -1137,8 +1137,10 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
         } else {
           q4_stage_x<1>(X, x, w.K, gm, tid, kStepConsumers, s_sum);
         }
-      } else {
+      } else if (gm) {
         q4_stage_x<1>(X, x, w.K, gm, tid, kStepConsumers, s_sum);
+      } else {  // no norm (O, DOWN): six items' loads in flight, one L2 round trip for K <= 12288
+        q4_stage_x<1, 6>(X, x, w.K, nullptr, tid, kStepConsumers, s_sum);
       }
       named_sync_id(kBarConsumers, kStepConsumers);
       // every thread forms 1/rms from the warps' sums (s_sum is rewritten only after the phase's barrier)

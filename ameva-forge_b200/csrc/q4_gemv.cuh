@@ -179,12 +179,11 @@ __device__ __forceinline__ uint32_t pack_s8x4(int a, int b, int c, int d) {
 // [0, nth) take part (nth a multiple of 64), 8 lanes per 32-element block.
 // x is read through L2 (it may have been written by other SMs this kernel).
 // ss_out[warp][m] receives each warp's sum of x^2 (for the RMSNorm).
-template <int MV>
+template <int MV, int U = 4>
 __device__ __forceinline__ void q4_stage_x(const Q4X<MV> &X, const float *x, int64_t ldx, const float *gamma, int tid,
                                            int nth, float *ss_out) {
   const int lane = tid & 31, warp = tid >> 5;
-  const int q = lane & 7;  // 4-element group of the block
-  constexpr int U = 4;     // items whose x (and gamma) loads are in flight together
+  const int q = lane & 7;  // 4-element group of the block; U items' x (and gamma) loads are in flight together
 #pragma unroll
   for (int m = 0; m < MV; ++m) {
     float ss = 0.0f;
