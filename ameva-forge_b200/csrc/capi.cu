@@ -178,6 +178,27 @@ void Ctx::check_device_error() {
   }
 }
 
+void Ctx::d2h_checked(void *dst, const void *src, uint64_t bytes) {
+  const uint64_t eoff = align_up(bytes, 16);
+  if (!gemv.err || eoff + sizeof(int) > staging_bytes) {
+    d2h(dst, src, bytes);
+    check_device_error();
+    return;
+  }
+  FG_CUDA(cudaMemcpyAsync(staging[0], src, bytes, cudaMemcpyDeviceToHost, stream));
+  FG_CUDA(cudaMemcpyAsync((char *)staging[0] + eoff, gemv.err, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  FG_CUDA(cudaStreamSynchronize(stream));
+  std::memcpy(dst, staging[0], bytes);
+  pending = 0;
+  int e = 0;
+  std::memcpy(&e, (const char *)staging[0] + eoff, sizeof(int));
+  if (e != 0) {
+    int zero = 0;
+    FG_CUDA(cudaMemcpy(gemv.err, &zero, sizeof(int), cudaMemcpyHostToDevice));
+    raise(FG_ERR_INTERNAL_GPU, "a kernel wait timed out on the device (code %d); results of the step are invalid", e);
+  }
+}
+
 // inv_freq tables for standalone RoPE calls, cached per (base, d).
 struct RopeCache {
   std::map<std::pair<float, int64_t>, float *> tables;

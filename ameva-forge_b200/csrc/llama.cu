@@ -935,8 +935,11 @@ int fg_llama_decode(fg_llama *m, const int32_t *ids, int32_t batch, int32_t *nex
   m->host_pos += 1;
   m->last_batch = batch;
   if (logits) read_logits(m, batch, logits);
-  if (next_ids) c.d2h(next_ids, m->ids, (uint64_t)batch * 4);
-  if (logits || next_ids) c.check_device_error();
+  if (next_ids) {
+    c.d2h_checked(next_ids, m->ids, (uint64_t)batch * 4);  // the tokens and the error word in one round trip
+  } else if (logits) {
+    c.check_device_error();
+  }
   FG_LAPI_END
 }
 

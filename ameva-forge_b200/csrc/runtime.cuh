@@ -114,6 +114,9 @@ struct Ctx {
   void d2h(void *dst, const void *src, uint64_t bytes);
   void sync();
   void check_device_error();  // raises if a kernel's bounded wait timed out
+  // d2h of a small result and the device error word in one stream synchronisation, then check_device_error's
+  // test on the word (falls back to the two steps when the result does not fit the staging buffer)
+  void d2h_checked(void *dst, const void *src, uint64_t bytes);
   void ensure_xh(uint64_t elems);  // grow gemv.xh (never during stream capture)
 };
 
