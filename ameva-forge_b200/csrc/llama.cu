@@ -352,7 +352,7 @@ void setup_exchange(fg_llama *m) {
   const int tp = m->tp;
   FG_REQUIRE(tp <= 8, FG_ERR_VALIDATION, "tensor parallel degree %d > 8", tp);
   const uint64_t part = align_up((uint64_t)2 * tp * m->H * 4, 256);
-  const uint64_t bytes = part + 256;  // pflag[8], key[8], kflag[8]
+  const uint64_t bytes = part + 256;  // flag words: key[8] at 8, kflag[8] at 16, the exchange counter at 24
   FG_CUDA(cudaMalloc(&m->xbuf, bytes));
   FG_CUDA(cudaMemset(m->xbuf, 0, bytes));
   cudaIpcMemHandle_t mine;

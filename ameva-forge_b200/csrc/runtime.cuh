@@ -277,7 +277,8 @@ struct StepArgs {
   const void *kv_maps = nullptr;
   // tensor parallelism (tp > 1): rank r's exchange region at xr[r] (a peer mapping for r != rank):
   // float part[2][tp][H] (partial sums of o_proj / down_proj by source rank, by exchange parity),
-  // then at byte xflags: u64 pflag[8] (exchange sequence per source), u64 key[8], u64 kflag[8].
+  // then at byte xflags the u64 flag words: key[8] at word 8, kflag[8] at word 16 (the greedy pick across
+  // vocabulary shards) and at word 24 the exchange counter (one add per CTA of every rank per exchange).
   int tp = 1, rank = 0;
   float *xr[8] = {};
   int64_t xflags = 0;
