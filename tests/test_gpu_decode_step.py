@@ -20,6 +20,8 @@ TINY2 = dict(O.LlamaShape(32000, 2048, 5632, 2, 32, 4).__dict__)   # head_dim 64
 L7B1 = dict(O.LlamaShape(32000, 4096, 11008, 1, 32, 32).__dict__)  # head_dim 128, MHA
 GQA4 = dict(O.LlamaShape(32000, 4096, 11008, 1, 32, 8).__dict__)   # head_dim 128, GQA 4:1 (tensor-core tiles)
 GQA2 = dict(O.LlamaShape(32000, 2048, 5632, 1, 32, 16).__dict__)   # head_dim 64, GQA 2:1 (CUDA-core tiles)
+GQA8D128 = dict(O.LlamaShape(32000, 4096, 11008, 1, 32, 4).__dict__)  # head_dim 128, GQA 8:1 (tensor-core tiles)
+GQA4D64 = dict(O.LlamaShape(32000, 2048, 5632, 1, 32, 8).__dict__)    # head_dim 64, GQA 4:1 (tensor-core tiles)
 
 
 def make(ctx, shape, seed, cap, layered=False):
@@ -45,6 +47,8 @@ def make(ctx, shape, seed, cap, layered=False):
     ("gqa4_d128_1layer", GQA4, 201),    # 7 tiles, the last partial
     ("gqa4_d128_short", GQA4, 3),       # one partial tile
     ("gqa2_d64_1layer", GQA2, 100),
+    ("gqa8_d128_1layer", GQA8D128, 150),
+    ("gqa4_d64_1layer", GQA4D64, 97),
 ])
 def test_step_kernel_equals_layered_decode(ctx, name, shape, plen):
     prompt = (np.arange(plen, dtype=np.int32) * 7919 % 32000).reshape(1, plen)
