@@ -126,10 +126,14 @@ __device__ __noinline__ bool wait_xcnt(const StepArgs &A, unsigned long long tar
   }
 }
 
-// Work index of this CTA's group grp: group-major (group 0 of every CTA, then group 1), so a phase with
-// fewer units than virtual CTAs puts at most one of them on an SM until every SM has one, instead of
-// filling both groups of the first SMs while the last ones idle.
-__device__ __forceinline__ int work_index(int grp) { return grp * (int)gridDim.x + (int)blockIdx.x; }
+// Work index of this CTA's group grp.  Single GPU: group-major (group 0 of every CTA, then group 1), so a
+// phase with fewer units than virtual CTAs puts at most one of them on an SM until every SM has one,
+// instead of filling both groups of the first SMs while the last ones idle.  The tensor-parallel instance
+// keeps CTA-major indices (2 b + grp).
+template <bool TP>
+__device__ __forceinline__ int work_index(int grp) {
+  return TP ? (int)blockIdx.x * kStepGroups + grp : grp * (int)gridDim.x + (int)blockIdx.x;
+}
 
 // Grid-wide barrier, one calling thread per CTA (after a CTA-wide barrier).
 // bar[0] counts arrivals and is never reset; bar[1] counts launches (the
@@ -795,7 +799,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   if (tid >= kStepConsumers) {
     const int grp = (tid - kStepConsumers) >> 5;
     if (lane != 0) return;
-    const int vk = work_index(grp);
+    const int vk = work_index<TP>(grp);
     unsigned char *ring = rings + grp * kStepStages * kQ4TileBytes;
     uint64_t *fl = full[grp], *em = empty[grp];
     const uint64_t pol = l2_evict_first_policy();
@@ -839,7 +843,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_decode_step(const __grid_co
   if (tid < (int)(sizeof(StepLayer) / 16))
     reinterpret_cast<uint4 *>(&s_layer[0])[tid] = reinterpret_cast<const uint4 *>(A.layers)[tid];
   const int grp = warp / kGroupWarps, gw = warp % kGroupWarps, gtid = tid % kGroupThreads;
-  const int vk = work_index(grp);
+  const int vk = work_index<TP>(grp);
   const int gbar = 1 + grp;
   unsigned char *ring = rings + grp * kStepStages * kQ4TileBytes;
   uint64_t *fl = full[grp], *em = empty[grp];
